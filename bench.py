@@ -1,0 +1,456 @@
+"""Benchmark of the sign-bit / FP8 attention forward on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload prefill|decode|paged_decode|longctx|cpu_ref]
+                    [--impl ours|reference] [--path auto|row|tile] [--gather]
+
+For N > 1 launch with torchrun (one rank per GPU, NCCL):
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench.py --gpus N --steps K --warmup W
+
+One step = one forward call (`hyperion_apex_kernel`) over one batch of the
+workload, inputs already in HBM.  Default workload: the causal prefill
+B4 H32 S_q=S_kv=4096 D128, bf16 output, per GPU; at N GPUs each rank runs its own
+(batch, head) shard of a global batch of 4*N sequences (weak scaling: no data-path
+collective; --gather adds the output all-gather as a separate measurement).
+
+Timing: W untimed warm-up steps; L2 flushed (256 MiB write) before every timed
+step; each step bracketed by CUDA events on the launch stream; the K steps
+bracketed by a barrier and torch.cuda.synchronize() on both sides; the max over
+ranks is reported.  `e2e` repeats the step through the public Python API with
+pinned host inputs: H2D copies, the forward and the D2H copy of O are inside the
+timed region.  `cpu_baseline` times the CPU oracle (the C restatement of the
+reference algorithm) on a bounded sample on this host's cores.
+
+`--impl reference` times the reference's own CPU path for this forward: the
+reference's kernel does not build and has no CPU attention, so that is the C
+restatement of its algorithm (oracle/), run on all host threads; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "hyperion-fa3-kernel-_b200"))
+sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+METRIC = "attn Q·KV-token pairs/s"
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# ---------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.gpus = set(gpu_indices)
+        self.proc = None
+        self.out = None
+
+    def start(self):
+        try:
+            self.out = open(os.path.join("/tmp", f"hyperion_clocks_{os.getpid()}.csv"), "w+")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.seek(0)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.read().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                idx = int(parts[0])
+            except ValueError:
+                continue
+            if self.gpus and idx not in self.gpus:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        self.out.close()
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------- workloads
+def build_workload(name, rank, world, device):
+    from hyperion_b200 import workloads as W
+
+    if name == "longctx":
+        H = W.CONFIGS["longctx"]["H"]
+        per = H // world
+        heads = range(rank * per, (rank + 1) * per)
+        wk = W.make_config("longctx", device=device, exact=False, heads=heads, seed=rank)
+        desc = f"longctx B1 H{H} S_q=S_kv=32768 D128 causal, heads {heads.start}-{heads.stop - 1} on this rank"
+        return wk, desc, "strong"
+    wk = W.make_config(name, device=device, exact=False, seed=rank)
+    c = W.CONFIGS[name]
+    if name == "paged_decode":
+        desc = (f"paged_decode B{c['B']} H{c['H']} D128 S_q=1, L~U[{c['lo']},{c['hi']}] seed 1, page {c['page']}, "
+                "random page pool, per GPU")
+    else:
+        desc = (f"{name} B{c['B']} H{c['H']} S_q={c['S_q']} S_kv={c['S_kv']} D128 "
+                f"{'causal' if c['causal'] else 'non-causal'}, per GPU")
+    return wk, desc, "weak"
+
+
+def call_forward(hyperion, wk, o, path="auto", **kw):
+    hyperion.hyperion_apex_kernel(wk.worklist, wk.total_work, wk.q, None, wk.k, None, wk.v, wk.v_scale, wk.ctx_lens,
+                                  wk.block_tables, o, wk.seq_q, wk.head_dim, wk.head_dim // 8, wk.block_size,
+                                  wk.num_blocks, wk.inv_sqrt_d, wk.causal, path=path, **kw)
+
+
+def roofline_numbers(wk, pairs, kernel_ms, pk):
+    """Dominant kernel: algorithmic work per launch / average launch time."""
+    if wk.seq_q == 1:
+        # decode: K (D/8 B) + V (D B) per pair, plus Q rows and O rows.
+        nbytes = pairs * wk.kv_bytes_per_pair() + wk.total_work * (wk.head_dim // 8) \
+            + wk.total_work * wk.head_dim * torch.tensor([], dtype=wk.o_dtype).element_size()
+        achieved = nbytes / (kernel_ms * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / pk["hbm_gbs"], "algorithmic_bytes_per_launch": nbytes}
+    flops = 2.0 * 2.0 * wk.head_dim * pairs  # QK (2D) + PV (2D) per pair
+    achieved = flops / (kernel_ms * 1e-3) / 1e12
+    return {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": achieved / pk["bf16_tflops"], "algorithmic_flops_per_launch": flops}
+
+
+def read_traffic(kernel_tag):
+    """DRAM bytes per launch from the committed ncu summary, if one exists:
+    a line `traffic_bytes_per_launch: <int>` in profiles/<kernel_tag>.md."""
+    path = os.path.join(REPO, "profiles", f"{kernel_tag}.md")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        for line in f:
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                try:
+                    return int(float(line.split(":", 1)[1].strip()))
+                except ValueError:
+                    return None
+    return None
+
+
+# ---------------------------------------------------------------------------- CPU baseline
+def cpu_baseline(wk_gpu, budget_s=12.0):
+    """Times the C oracle on a sample of this workload's (batch, head) rows on all host
+    threads.  Returns (pairs/s, threads, description)."""
+    from oracle import oracle as O
+    from hyperion_b200 import workloads as W
+
+    threads = O.lib().oracle_max_threads()
+    n_bh = wk_gpu.n_bh
+    bh_order = torch.randperm(n_bh, generator=torch.Generator().manual_seed(0)).tolist()
+    # Rows per oracle call: enough work items to keep every host thread busy.
+    per_call = max(1, (4 * threads + wk_gpu.seq_q - 1) // wk_gpu.seq_q)
+    done_pairs, spent, used = 0, 0.0, 0
+    pos = 0
+    while pos < n_bh:
+        rows = bh_order[pos: pos + per_call]
+        pos += len(rows)
+        sub = _subset_rows(wk_gpu, rows)
+        t0 = time.perf_counter()
+        O.forward_workload_c(sub, nthreads=threads)
+        spent += time.perf_counter() - t0
+        done_pairs += sub.pairs()
+        used += len(rows)
+        if spent > budget_s * 0.5:
+            break
+    desc = (f"{used} of {n_bh} (batch, head) rows of this workload with all their query rows, "
+            f"{per_call} rows per call, {spent:.1f} s")
+    return done_pairs / spent, threads, desc
+
+
+def _subset_rows(wk, rows):
+    """The listed (batch, head) rows of a workload, with every query row of each, as a
+    contiguous CPU workload (their keys gathered from the pool on the device)."""
+    from hyperion_b200 import workloads as W
+
+    cap = wk.num_blocks * wk.block_size
+    lens = [min(int(wk.ctx_lens[bh]), cap) for bh in rows]
+    Lmax = max(max(lens), 1)
+    W_ = wk.head_dim // 32
+    kk = torch.zeros(len(rows) * Lmax, W_, dtype=torch.int32, device=wk.k.device)
+    vv = torch.zeros(len(rows) * Lmax, wk.head_dim, dtype=torch.uint8, device=wk.k.device)
+    qq, sc = [], []
+    vs = wk.v_scale
+    for i, (bh, L) in enumerate(zip(rows, lens)):
+        t = torch.arange(L, device=wk.k.device)
+        page = t // wk.block_size
+        ids = wk.block_tables[bh].to(torch.int64)[page] if wk.block_tables.numel() else bh * wk.num_blocks + page
+        slots = ids * wk.block_size + t % wk.block_size
+        kk[i * Lmax: i * Lmax + L] = wk.k[slots]
+        vv[i * Lmax: i * Lmax + L] = wk.v[slots]
+        qq.append(wk.q[bh * wk.seq_q:(bh + 1) * wk.seq_q])
+        sc.append(vs.reshape(-1)[0] if vs.numel() == 1 else vs[bh % vs.numel()])
+    scale = torch.stack(sc).float()
+    if scale.numel() == kk.shape[0]:  # keep the per-row scale unambiguous
+        scale = torch.cat([scale, scale[:1]])
+    wl = W.dense_worklist(len(rows), wk.seq_q, "cpu")
+    if wk.seq_q == 1:
+        wl[:, 0] = 0
+    return W.Workload(name=wk.name + "_sample", worklist=wl, q=torch.cat(qq).cpu(), k=kk.cpu(), v=vv.cpu(),
+                      v_scale=scale.cpu(), ctx_lens=torch.tensor(lens, dtype=torch.int32),
+                      block_tables=torch.zeros(0, dtype=torch.int32), seq_q=wk.seq_q, head_dim=wk.head_dim,
+                      block_size=Lmax, num_blocks=1, causal=wk.causal, o_dtype=torch.float32, batch=1,
+                      heads=len(rows), inv_sqrt_d=wk.inv_sqrt_d)
+
+
+# ---------------------------------------------------------------------------- arms
+def run_reference(args):
+    rank, world, local = dist_env()
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+
+    dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    wk, desc, _ = build_workload(args.workload, 0, 1, dev)
+    threads = O.lib().oracle_max_threads()
+    budget = max(2.0, 150.0 / max(1, args.steps + args.warmup))
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, threads, sample = cpu_baseline(wk, budget_s=budget)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    out = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "pairs/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": desc},
+        "cpu_baseline": {"value": value, "unit": "pairs/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "pairs/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's CUDA kernel does not build and it has no CPU attention path; this is the C "
+                "restatement of its algorithm (oracle/hyperion_oracle.c) on all host threads",
+    }
+    print(json.dumps(out))
+    return 0
+
+
+def run_ours(args):
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+    import hyperion_b200 as hyperion
+
+    wk, desc, scaling = build_workload(args.workload, rank, world, dev)
+    o = wk.new_output()
+    pairs = wk.pairs()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+
+    for _ in range(args.warmup):
+        call_forward(hyperion, wk, o, path=args.path)
+    torch.cuda.synchronize()
+    info = hyperion.last_call_info()
+    errs = hyperion.read_device_errors(dev, clear=True)
+
+    # nvidia-smi samples every 200 ms, longer than a short timed region: the sampler
+    # starts before a >= 1.5 s sustained run of the same step that leads straight
+    # into the timed steps, and stops after them.
+    clocks = ClockSampler([local] if world == 1 else list(range(world)))
+    if rank == 0:
+        clocks.start()
+    t_end = time.perf_counter() + 1.5
+    n_sus = 0
+    while time.perf_counter() < t_end or n_sus < 2:
+        flush.fill_(n_sus & 0xFF)
+        call_forward(hyperion, wk, o, path=args.path)
+        n_sus += 1
+        if n_sus % 4 == 0:
+            torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        starts[i].record(stream)
+        call_forward(hyperion, wk, o, path=args.path)
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(step_ms)
+    clk = clocks.stop() if rank == 0 else None
+
+    # e2e through the public API with pinned host buffers.
+    host = {k: getattr(wk, k).cpu().pin_memory() for k in ("worklist", "q", "k", "v", "v_scale", "ctx_lens",
+                                                           "block_tables")}
+    dbuf = {k: torch.empty_like(getattr(wk, k)) for k in host}
+    o_host = torch.empty(o.shape, dtype=o.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = o_host.numel() * o_host.element_size()
+
+    def e2e_step():
+        for k_, t in host.items():
+            dbuf[k_].copy_(t, non_blocking=True)
+        sub = type(wk)(**{**wk.__dict__, **dbuf})
+        call_forward(hyperion, sub, o, path=args.path)
+        o_host.copy_(o, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e_start.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e_start.elapsed_time(e_end)
+
+    gather_ms = None
+    if args.gather and world > 1:
+        out_all = torch.empty((world,) + tuple(o.shape), dtype=o.dtype, device=dev)
+        pg.all_gather_into_tensor(out_all, o)
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        g0.record(stream)
+        for _ in range(args.steps):
+            pg.all_gather_into_tensor(out_all, o)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        gather_ms = g0.elapsed_time(g1) / args.steps
+
+    vals = torch.tensor([total_ms, e2e_ms, float(pairs), gather_ms or 0.0], dtype=torch.float64, device=dev)
+    if pg is not None:
+        mx = vals.clone()
+        pg.all_reduce(mx, op=pg.ReduceOp.MAX)
+        sm = vals.clone()
+        pg.all_reduce(sm, op=pg.ReduceOp.SUM)
+        total_ms_max, e2e_ms_max, gather_max = float(mx[0]), float(mx[1]), float(mx[3])
+        pairs_all = float(sm[2])
+    else:
+        total_ms_max, e2e_ms_max, gather_max = total_ms, e2e_ms, gather_ms or 0.0
+        pairs_all = float(pairs)
+
+    if rank == 0:
+        pk, pk_src = peaks()
+        kernel_ms = total_ms / args.steps
+        roof = roofline_numbers(wk, pairs, kernel_ms, pk)
+        roof["peak_source"] = pk_src
+        kernel_tag = f"{info['path'] or 'row'}_kernel_{args.workload}"
+        roof["kernel"] = f"{info['path']} kernel"
+        roof["traffic"] = read_traffic(kernel_tag)
+        if world == 1 and not args.no_cpu_baseline:
+            v_cpu, cores, sample = cpu_baseline(wk)
+            cpu = {"value": v_cpu, "unit": "pairs/s", "cores": cores, "kind": "port", "sample": sample}
+        else:
+            cpu = None
+        value = pairs_all * args.steps / (total_ms_max * 1e-3)
+        e2e_val = pairs_all * args.steps / (e2e_ms_max * 1e-3)
+        c = {
+            "workload": desc,
+            "global_batch": wk.batch * world if scaling == "weak" else wk.batch,
+            "heads": wk.heads if scaling == "weak" else wk.heads * world,
+            "seq_len": wk.seq_q if wk.seq_q > 1 else int(wk.ctx_lens.max()),
+            "head_dim": wk.head_dim,
+            "causal": wk.causal,
+            "parallelism": f"(batch, head) shards x{world}, no data-path collective",
+            "l2": "flushed before every timed step (256 MiB write)",
+            "path": info["path"],
+            "kv_splits": info["splits"],
+        }
+        out = {
+            "metric": METRIC, "value": value, "unit": "pairs/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms_max / args.steps, "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None,
+            "dtype": "sign-bit QK (e4m3 +-1 MMA, exact int) / f16 PV" if info["path"] == "tile"
+                     else "sign-bit QK (popc, exact int) / f32 PV",
+            "data": "synthetic: seeded random sign bits for Q/K, N(0,1) V as FP8 e4m3 with per-head scale",
+            "config": c, "pairs_per_step": pairs_all,
+            "roofline": roof, "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": "pairs/s", "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world},
+            "gpu_launches": info["kernels"] * args.steps,
+            "clocks": clk, "device_errors": errs,
+            "step_ms_min": min(step_ms), "step_ms_max": max(step_ms),
+        }
+        if gather_ms is not None:
+            out["gather_ms"] = gather_max
+        print(json.dumps(out))
+    if pg is not None:
+        pg.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="prefill",
+                    choices=["prefill", "decode", "paged_decode", "longctx", "cpu_ref"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--path", default="auto", choices=["auto", "row", "tile"])
+    ap.add_argument("--gather", action="store_true", help="also time the NCCL all-gather of O (N > 1)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

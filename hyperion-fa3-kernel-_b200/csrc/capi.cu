@@ -1,0 +1,336 @@
+// capi.cu -- the C ABI declared in include/hyperion_b200.h.
+//
+// Host side of the forward: validates every pointer and size the reference's
+// pybind boundary would have taken on trust (hyperion_fa3_production_final.py:598-601),
+// derives the launch from the device (the reference hard-codes grid = min(2*SM, 256),
+// block 256, :907-912), zeroes the per-call work counter on the caller's stream
+// (the reference needs a separate reset launch, :73-77 / :905) and enqueues the
+// row kernel or the tcgen05 tile kernel.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "row_kernel.cuh"
+#include "tile_kernel.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+thread_local int32_t g_last_call[4] = {0, 0, 0, 0};
+
+int fail(int code, const char* msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+  return HYPERION_ERR_CUDA;
+}
+
+struct DevInfo {
+  bool ready = false;
+  int n_sm = 0;
+  int row_ctas_128 = 1, row_ctas_256 = 1;
+  int row_smem_128 = 0, row_smem_256 = 0;
+  int tile_ctas = 0, tile_smem = 0;
+  bool tile_ok = false;
+};
+
+constexpr int kMaxDevices = 64;
+DevInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+template <int D>
+int setup_row(int& ctas, int& smem) {
+  smem = (int)sizeof(hyp::row::Smem<D>);
+  cudaError_t e = cudaFuncSetAttribute(hyp::row::row_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(row)");
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, hyp::row::row_fwd_kernel<D>, hyp::row::kThreads, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor(row)");
+  if (ctas < 1) ctas = 1;
+  return HYPERION_OK;
+}
+
+int get_dev(const DevInfo** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(HYPERION_ERR_UNSUPPORTED, "device ordinal out of range");
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DevInfo& di = g_dev[dev];
+  if (!di.ready) {
+    e = cudaDeviceGetAttribute(&di.n_sm, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    int rc = setup_row<128>(di.row_ctas_128, di.row_smem_128);
+    if (rc) return rc;
+    rc = setup_row<256>(di.row_ctas_256, di.row_smem_256);
+    if (rc) return rc;
+    rc = hyp::tile::setup(di.tile_ctas, di.tile_smem);
+    di.tile_ok = (rc == HYPERION_OK);
+    if (!di.tile_ok) {
+      di.tile_ctas = 0;
+      cudaGetLastError();
+    }
+    di.ready = true;
+  }
+  *out = &di;
+  return HYPERION_OK;
+}
+
+// KV splits per item of the row kernel.  Enough units that every CTA slot gets
+// about 16 of them (balance), no split below 512 keys, none above 8192 keys when
+// the table allows longer contexts, and at most 16.
+int choose_splits(const DevInfo& di, int D, int total_work, long long max_keys) {
+  if (total_work <= 0) return 1;
+  const int ctas = (D == 256) ? di.row_ctas_256 : di.row_ctas_128;
+  const long long target = (long long)di.n_sm * ctas * 16;
+  long long ns = 1;
+  if (total_work < target) ns = (target + total_work - 1) / total_work;
+  ns = std::max<long long>(ns, (max_keys + 8191) / 8192);
+  ns = std::min<long long>(ns, std::max<long long>(1, max_keys / 512));
+  ns = std::min<long long>(ns, 16);
+  return (int)std::max<long long>(ns, 1);
+}
+
+size_t partial_bytes(int total_work, int n_split, int D) {
+  if (n_split <= 1) return 0;
+  return (size_t)total_work * n_split * (2 + D) * sizeof(float);
+}
+
+size_t workspace_needed(const DevInfo& di, int total_work, int D, int block_size, int num_blocks) {
+  const long long max_keys = (long long)std::max(block_size, 1) * std::max(num_blocks, 1);
+  // Worst case over the automatic choice and any forced num_splits (capped at 16).
+  const int ns = std::max(choose_splits(di, D, total_work, max_keys), 16);
+  return hyp::kWsPartials + partial_bytes(total_work, ns, D);
+}
+
+struct Call {
+  hyp::FwdParams p;
+  int total_work;
+};
+
+}  // namespace
+
+extern "C" {
+
+int32_t hyperion_version(void) { return 1 * 10000 + 0 * 100 + 0; }
+
+const char* hyperion_last_error_string(void) { return g_last_error.c_str(); }
+
+int hyperion_last_call_info(int32_t* out, int32_t n) {
+  if (out == nullptr) return fail(HYPERION_ERR_INVALID_ARG, "out is NULL");
+  for (int i = 0; i < n && i < 4; ++i) out[i] = g_last_call[i];
+  return HYPERION_OK;
+}
+
+size_t hyperion_workspace_bytes(int32_t total_work, int32_t head_dim, int32_t block_size, int32_t num_blocks) {
+  const DevInfo* di = nullptr;
+  if (get_dev(&di) != HYPERION_OK) return 0;
+  if (total_work < 0) total_work = 0;
+  return workspace_needed(*di, total_work, head_dim == 256 ? 256 : 128, block_size, num_blocks);
+}
+
+int hyperion_launch_info(int32_t* out, int32_t n) {
+  const DevInfo* di = nullptr;
+  const int rc = get_dev(&di);
+  if (rc) return rc;
+  const int32_t v[7] = {di->n_sm, di->row_ctas_128, di->row_smem_128, di->tile_ctas, di->tile_smem,
+                        di->row_ctas_256, di->tile_ok ? 1 : 0};
+  for (int i = 0; i < n && i < 7; ++i) out[i] = v[i];
+  return HYPERION_OK;
+}
+
+int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const uint32_t* Q, const float* Q_scale,
+                            const uint32_t* K_cache, const float* K_scale, const uint8_t* V_cache,
+                            const float* V_scale, const int32_t* context_lens, const int32_t* block_tables,
+                            void* O, int32_t seq_q, int32_t head_dim, int32_t k_packed_bytes, int32_t block_size,
+                            int32_t num_blocks, float inv_sqrt_d, int32_t causal, const hyperion_extents* ext,
+                            const hyperion_options* opt, void* workspace, size_t workspace_bytes, void* stream) {
+  (void)Q_scale;
+  (void)K_scale;
+  if (ext == nullptr) return fail(HYPERION_ERR_INVALID_ARG, "ext (sizes) is NULL");
+  if (total_work < 0) return fail(HYPERION_ERR_INVALID_ARG, "total_work < 0");
+  if (head_dim != 128 && head_dim != 256)
+    return fail(HYPERION_ERR_UNSUPPORTED, "head_dim must be 128 or 256");
+  if (k_packed_bytes != head_dim / 8)
+    return fail(HYPERION_ERR_INVALID_ARG, "k_packed_bytes must be head_dim/8 (sign-bit K)");
+  if (seq_q < 1) return fail(HYPERION_ERR_INVALID_ARG, "seq_q < 1");
+  if (block_size < 1) return fail(HYPERION_ERR_INVALID_ARG, "block_size < 1");
+  if (num_blocks < 1) return fail(HYPERION_ERR_INVALID_ARG, "num_blocks < 1");
+  if (!std::isfinite(inv_sqrt_d)) return fail(HYPERION_ERR_INVALID_ARG, "inv_sqrt_d is not finite");
+  if (ext->n_bh < 1) return fail(HYPERION_ERR_INVALID_ARG, "n_bh (context_lens numel) < 1");
+  if (ext->pool_rows < 1) return fail(HYPERION_ERR_INVALID_ARG, "pool_rows < 1");
+  if (ext->v_scale_numel < 1) return fail(HYPERION_ERR_INVALID_ARG, "V_scale is empty");
+  if (ext->o_dtype != HYPERION_DTYPE_F16 && ext->o_dtype != HYPERION_DTYPE_BF16 && ext->o_dtype != HYPERION_DTYPE_F32)
+    return fail(HYPERION_ERR_INVALID_ARG, "o_dtype is not F16, BF16 or F32");
+  const bool paged = ext->block_tables_numel != 0;
+  if (paged) {
+    if (block_tables == nullptr) return fail(HYPERION_ERR_INVALID_ARG, "block_tables is NULL but numel > 0");
+    if (ext->block_tables_numel < (int64_t)ext->n_bh * num_blocks)
+      return fail(HYPERION_ERR_INVALID_ARG, "block_tables numel < n_bh * num_blocks");
+  }
+  if (workspace == nullptr) return fail(HYPERION_ERR_WORKSPACE, "workspace is NULL");
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+    return fail(HYPERION_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  if (total_work == 0) {
+    g_last_call[0] = g_last_call[1] = g_last_call[2] = g_last_call[3] = 0;
+    return HYPERION_OK;
+  }
+  if (!worklist || !Q || !K_cache || !V_cache || !V_scale || !context_lens || !O)
+    return fail(HYPERION_ERR_INVALID_ARG, "a tensor pointer is NULL");
+  if (reinterpret_cast<uintptr_t>(worklist) % 16 != 0)
+    return fail(HYPERION_ERR_INVALID_ARG, "worklist must be 16-byte aligned (int4 rows)");
+  if (reinterpret_cast<uintptr_t>(K_cache) % 16 != 0 || reinterpret_cast<uintptr_t>(V_cache) % 16 != 0)
+    return fail(HYPERION_ERR_INVALID_ARG, "K_cache and V_cache must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(Q) % 16 != 0) return fail(HYPERION_ERR_INVALID_ARG, "Q must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(O) % 16 != 0) return fail(HYPERION_ERR_INVALID_ARG, "O must be 16-byte aligned");
+
+  const DevInfo* di = nullptr;
+  int rc = get_dev(&di);
+  if (rc) return rc;
+
+  const int path_req = opt ? opt->path : HYPERION_PATH_AUTO;
+  if (path_req != HYPERION_PATH_AUTO && path_req != HYPERION_PATH_ROW && path_req != HYPERION_PATH_TILE)
+    return fail(HYPERION_ERR_INVALID_ARG, "unknown path");
+
+  hyp::FwdParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.worklist = reinterpret_cast<const int4*>(worklist);
+  p.total_work = total_work;
+  p.q = Q;
+  p.k = K_cache;
+  p.v = V_cache;
+  p.v_scale = V_scale;
+  p.v_scale_numel = ext->v_scale_numel;
+  p.v_scale_mode = (ext->v_scale_numel == 1) ? 0 : (ext->v_scale_numel == ext->pool_rows ? 2 : 1);
+  p.ctx_lens = context_lens;
+  p.n_bh = ext->n_bh;
+  p.block_tables = paged ? block_tables : nullptr;
+  p.pool_rows = ext->pool_rows;
+  p.pool_blocks = ext->pool_rows / block_size;
+  p.o = O;
+  p.o_dtype = ext->o_dtype;
+  p.seq_q = seq_q;
+  p.head_dim = head_dim;
+  p.block_size = block_size;
+  p.num_blocks = num_blocks;
+  p.inv_sqrt_d = inv_sqrt_d;
+  p.causal = causal ? 1 : 0;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.counters = reinterpret_cast<uint32_t*>(ws + hyp::kWsCounters);
+  p.err = reinterpret_cast<uint32_t*>(ws + hyp::kWsError);
+  p.partials = reinterpret_cast<float*>(ws + hyp::kWsPartials);
+  p.debug_scores = opt ? opt->debug_scores : nullptr;
+  p.debug_ld = opt ? opt->debug_ld : 0;
+  if (p.debug_scores && p.debug_ld < 1) return fail(HYPERION_ERR_INVALID_ARG, "debug_ld < 1");
+
+  g_last_call[0] = g_last_call[1] = g_last_call[2] = g_last_call[3] = 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const long long max_keys = (long long)block_size * num_blocks;
+
+  // Kernel choice: the tile kernel needs head_dim 128, a per-tensor / per-head V
+  // scale and enough query rows per (batch, head) to fill 128-row tiles.
+  const bool tile_fits = di->tile_ok && head_dim == 128 && p.v_scale_mode != 2;
+  int path = path_req;
+  if (path == HYPERION_PATH_AUTO) path = (tile_fits && seq_q >= 64) ? HYPERION_PATH_TILE : HYPERION_PATH_ROW;
+  if (path == HYPERION_PATH_TILE && !tile_fits)
+    return fail(HYPERION_ERR_UNSUPPORTED,
+                "tile path needs head_dim 128, a per-tensor or per-head V scale and a device that loaded it");
+
+  cudaError_t e = cudaMemsetAsync(ws + hyp::kWsCounters, 0, 64, st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(counters)");
+
+  if (path == HYPERION_PATH_TILE) {
+    int grid = 0;
+    rc = hyp::tile::launch(p, di->n_sm, di->tile_ctas, di->tile_smem, st, &grid);
+    if (rc) return rc;
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "tile kernel launch");
+    g_last_call[0] = HYPERION_PATH_TILE;
+    g_last_call[1] = 1;
+    g_last_call[2] = 1;
+    g_last_call[3] = grid;
+    return HYPERION_OK;
+  }
+
+  int ns = (opt && opt->num_splits > 0) ? std::min(opt->num_splits, 16) : choose_splits(*di, head_dim, total_work, max_keys);
+  const size_t need = hyp::kWsPartials + partial_bytes(total_work, ns, head_dim);
+  if (workspace_bytes < need) return fail(HYPERION_ERR_WORKSPACE, "workspace smaller than hyperion_workspace_bytes()");
+  p.n_split = ns;
+  const long long units = (long long)total_work * ns;
+  if (units > 0x7fffffffLL) return fail(HYPERION_ERR_UNSUPPORTED, "too many work units");
+  const int ctas = (head_dim == 256) ? di->row_ctas_256 : di->row_ctas_128;
+  const int smem = (head_dim == 256) ? di->row_smem_256 : di->row_smem_128;
+  const int grid = (int)std::min<long long>(units, (long long)di->n_sm * ctas);
+  if (head_dim == 256) {
+    hyp::row::row_fwd_kernel<256><<<grid, hyp::row::kThreads, smem, st>>>(p, (int)units);
+  } else {
+    hyp::row::row_fwd_kernel<128><<<grid, hyp::row::kThreads, smem, st>>>(p, (int)units);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "row kernel launch");
+  if (ns > 1) {
+    if (head_dim == 256) {
+      hyp::row::row_combine_kernel<256><<<total_work, 128, 0, st>>>(p);
+    } else {
+      hyp::row::row_combine_kernel<128><<<total_work, 128, 0, st>>>(p);
+    }
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
+  }
+  g_last_call[0] = HYPERION_PATH_ROW;
+  g_last_call[1] = ns;
+  g_last_call[2] = ns > 1 ? 2 : 1;
+  g_last_call[3] = grid;
+  return HYPERION_OK;
+}
+
+int hyperion_apex_kernel(const int32_t* worklist, int32_t total_work, const uint32_t* Q, const float* Q_scale,
+                         const uint32_t* K_cache, const float* K_scale, const uint8_t* V_cache, const float* V_scale,
+                         const int32_t* context_lens, const int32_t* block_tables, void* O, int32_t seq_q,
+                         int32_t head_dim, int32_t k_packed_bytes, int32_t block_size, int32_t num_blocks,
+                         float inv_sqrt_d, int32_t causal, const hyperion_extents* ext, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  return hyperion_apex_kernel_ex(worklist, total_work, Q, Q_scale, K_cache, K_scale, V_cache, V_scale, context_lens,
+                                 block_tables, O, seq_q, head_dim, k_packed_bytes, block_size, num_blocks, inv_sqrt_d,
+                                 causal, ext, nullptr, workspace, workspace_bytes, stream);
+}
+
+int hyperion_reset_counter(void* workspace, size_t workspace_bytes, void* stream) {
+  if (workspace == nullptr || workspace_bytes < hyp::kWsPartials)
+    return fail(HYPERION_ERR_WORKSPACE, "workspace missing or too small");
+  cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(workspace) + hyp::kWsCounters, 0, 64,
+                                  static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(counters)");
+  return HYPERION_OK;
+}
+
+int hyperion_read_device_errors(void* workspace, size_t workspace_bytes, void* stream, uint32_t* flags,
+                                int32_t clear) {
+  if (workspace == nullptr || workspace_bytes < hyp::kWsPartials || flags == nullptr)
+    return fail(HYPERION_ERR_INVALID_ARG, "workspace or flags missing");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t v = 0;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaError_t e = cudaMemcpyAsync(&v, ws + hyp::kWsError, sizeof(v), cudaMemcpyDeviceToHost, st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(error word)");
+  e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  *flags = v;
+  if (clear) {
+    e = cudaMemsetAsync(ws + hyp::kWsError, 0, sizeof(uint32_t), st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(error word)");
+    e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  }
+  return HYPERION_OK;
+}
+
+}  // extern "C"

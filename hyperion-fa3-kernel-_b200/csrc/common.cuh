@@ -1,0 +1,285 @@
+// common.cuh -- device helpers shared by the row (split-KV) and tile (tcgen05) kernels.
+//
+// Everything here is sm_100a PTX or plain CUDA: mbarrier phase waits with a clock
+// bound, bulk (TMA engine) global->shared copies, the reference's FP8 e4m3 decode
+// as integer bit moves, and the sign-bit score.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+#include "hyperion_b200.h"
+
+namespace hyp {
+
+// EXP_CLAMP of the reference (hyperion_fa3_production_final.py:59): every softmax
+// exponent is max(x, -80) before exp.
+constexpr float kExpClamp = -80.0f;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// A bounded wait gives up after this many SM clock cycles (about 1 s at 1.9 GHz),
+// raises HYPERION_DEVERR_WAIT_TIMEOUT and lets the CTA unwind.
+constexpr long long kWaitCycles = 2000000000LL;
+
+// Workspace layout (byte offsets).  The counters block is zeroed on the stream at
+// the start of every forward; the error word is sticky until read and cleared.
+constexpr size_t kWsCounters = 0;     // uint32[16]: [0] row-kernel ticket, [1] tile-kernel ticket
+constexpr size_t kWsError = 64;       // uint32 error flags
+constexpr size_t kWsPartials = 256;   // float partials of the split-KV row kernel
+
+struct FwdParams {
+  const int4* worklist;
+  int total_work;
+  const uint32_t* q;      // [n_bh*seq_q, W]
+  const uint32_t* k;      // [pool_rows, W]
+  const uint8_t* v;       // [pool_rows, D]
+  const float* v_scale;
+  int v_scale_mode;       // 0 per tensor, 1 index bh % numel, 2 per slot
+  long long v_scale_numel;
+  const int* ctx_lens;
+  int n_bh;
+  const int* block_tables;  // nullptr -> contiguous
+  long long pool_rows;
+  long long pool_blocks;    // pool_rows / block_size
+  void* o;
+  int o_dtype;
+  int seq_q, head_dim, block_size, num_blocks;
+  float inv_sqrt_d;
+  int causal;
+  uint32_t* counters;
+  uint32_t* err;
+  float* partials;
+  int n_split;
+  int* debug_scores;
+  long long debug_ld;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void raise_error(uint32_t* err, uint32_t flag) {
+  atomicOr(err, flag);
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase with parity `parity` to complete.  Returns false (and sets
+// *abort) when the CTA is aborting or the wait exceeded kWaitCycles; the first
+// waiter that times out records HYPERION_DEVERR_WAIT_TIMEOUT.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          uint32_t* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      raise_error(err, HYPERION_DEVERR_WAIT_TIMEOUT);
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
+// Bounded wait that ignores the abort flag: used on the way out of an aborted CTA
+// to let copies already in flight land before the CTA's shared memory is released.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) return;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Bulk copy global -> shared through the TMA engine (no tensor map: plain bytes).
+// Both addresses 16-byte aligned, size a multiple of 16.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Same copy with an L2 eviction-priority hint for data read once (KV streams).
+__device__ __forceinline__ void bulk_g2s_stream(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                                uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+      "%4;" ::"r"(smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Arithmetic
+// ---------------------------------------------------------------------------
+// 2^x with the hardware approximation (MUFU.EX2).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// exp(max(x, EXP_CLAMP)) as the reference writes it (__expf(fmaxf(x, EXP_CLAMP))).
+__device__ __forceinline__ float exp_clamped(float x) {
+  return ex2_approx(fmaxf(x, kExpClamp) * kLog2e);
+}
+
+// FP8 e4m3 -> f32 bit pattern scaled by 2^-120: sign to bit 31, the 7 exponent and
+// mantissa bits to bits 26..20.  For every code this is exactly
+// fp8_e4m3_to_fp32(code) * 2^-120 of the reference (hyperion_fa3_production_final.py:122-141),
+// including subnormals (exponent field 0 -> f32 denormals) and the exponent-15
+// codes 0x7F / 0xFF, which the reference decodes as +-480.
+__device__ __forceinline__ float fp8_bits_to_f32_scaled(uint32_t byte_in_low_bits) {
+  const uint32_t b = byte_in_low_bits & 0xFFu;
+  return __uint_as_float(((b & 0x80u) << 24) | ((b & 0x7Fu) << 20));
+}
+constexpr float kTwoPow120 = 1.329227995784916e+36f;  // 2^120
+
+// Two FP8 e4m3 codes held in bytes 1 and 3 of `v` -> f16x2 {byte1, byte3}, each
+// equal to the reference decode divided by 256 (exact: f16 covers e4m3 / 256).
+__device__ __forceinline__ uint32_t fp8x2_odd_to_f16x2_div256(uint32_t v) {
+  return ((v >> 1) & 0x3F803F80u) | (v & 0x80008000u);
+}
+// Bytes 0 and 2 of `v` -> f16x2 {byte0, byte2}, decode / 256.
+__device__ __forceinline__ uint32_t fp8x2_even_to_f16x2_div256(uint32_t v) {
+  return ((v << 7) & 0x3F803F80u) | ((v << 8) & 0x80008000u);
+}
+
+// Integer score D - 2*popcount(q XOR k) over W 32-bit words.
+template <int W>
+__device__ __forceinline__ int sign_score(const uint32_t (&q)[W], const uint32_t* k) {
+  int p = 0;
+#pragma unroll
+  for (int i = 0; i < W; ++i) p += __popc(q[i] ^ k[i]);
+  return W * 32 - 2 * p;
+}
+
+__device__ __forceinline__ float v_scale_for(const FwdParams& p, int bh, long long slot) {
+  switch (p.v_scale_mode) {
+    case 0: return __ldg(p.v_scale);
+    case 1: return __ldg(p.v_scale + (bh % p.v_scale_numel));
+    default: return __ldg(p.v_scale + slot);
+  }
+}
+
+// Page id of page `page` of (batch, head) row `bh`, or -1 when it lies outside the pool.
+__device__ __forceinline__ long long page_block_id(const FwdParams& p, int bh, int page) {
+  long long id;
+  if (p.block_tables == nullptr) {
+    id = (long long)bh * p.num_blocks + page;
+  } else {
+    id = __ldg(p.block_tables + (long long)bh * p.num_blocks + page);
+  }
+  if (id < 0 || id >= p.pool_blocks) return -1;
+  return id;
+}
+
+template <typename T>
+__device__ __forceinline__ T to_out(float x);
+template <>
+__device__ __forceinline__ float to_out<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __half to_out<__half>(float x) { return __float2half_rn(x); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 to_out<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+__device__ __forceinline__ void store_out(void* o, int dtype, long long idx, float x) {
+  if (dtype == HYPERION_DTYPE_F32) {
+    static_cast<float*>(o)[idx] = x;
+  } else if (dtype == HYPERION_DTYPE_BF16) {
+    static_cast<__nv_bfloat16*>(o)[idx] = __float2bfloat16_rn(x);
+  } else {
+    static_cast<__half*>(o)[idx] = __float2half_rn(x);
+  }
+}
+
+// Resolved key range of one work item: keys [0, kv_end) after the context length,
+// the block-table width and the causal bound; `valid` false when the item itself
+// is out of range (its output row is then not written).
+struct ItemInfo {
+  int bh;
+  int q_idx;
+  int kv_end;
+  bool valid;
+};
+
+__device__ __forceinline__ ItemInfo resolve_item(const FwdParams& p, int item) {
+  ItemInfo r;
+  const int4 wl = __ldg(p.worklist + item);
+  r.q_idx = wl.x;
+  r.bh = wl.y;
+  r.valid = (r.bh >= 0 && r.bh < p.n_bh && r.q_idx >= 0 && r.q_idx < p.seq_q);
+  r.kv_end = 0;
+  if (!r.valid) return r;
+  int ctx = __ldg(p.ctx_lens + r.bh);
+  const long long cap = (long long)p.num_blocks * p.block_size;
+  if (ctx < 0) ctx = 0;
+  if ((long long)ctx > cap) ctx = (int)cap;
+  if (p.causal && ctx > r.q_idx + 1) ctx = r.q_idx + 1;
+  r.kv_end = ctx;
+  return r;
+}
+
+// Raises the item-level error flags once per item (called by one thread).
+__device__ __forceinline__ void check_item_errors(const FwdParams& p, int item) {
+  const int4 wl = __ldg(p.worklist + item);
+  const int q_idx = wl.x, bh = wl.y;
+  if (!(bh >= 0 && bh < p.n_bh && q_idx >= 0 && q_idx < p.seq_q)) {
+    raise_error(p.err, HYPERION_DEVERR_BAD_ITEM);
+    return;
+  }
+  const int ctx = __ldg(p.ctx_lens + bh);
+  if (ctx < 0) raise_error(p.err, HYPERION_DEVERR_NEG_CTX);
+  if ((long long)ctx > (long long)p.num_blocks * p.block_size) raise_error(p.err, HYPERION_DEVERR_CTX_OVERFLOW);
+}
+
+}  // namespace hyp

@@ -1,0 +1,382 @@
+// row_kernel.cuh -- split-KV row kernel: one work item (one query row of one
+// (batch, head)) against a contiguous or paged KV cache, on CUDA cores.
+//
+// This is the decode path (S_q = 1, the HBM-bound case) and the general path for
+// any worklist.  It replaces the reference's persistent kernel
+// (hyperion_fa3_production_final.py:268-596):
+//   * work stealing: a per-call ticket in the caller's workspace instead of the
+//     __device__ g_work_counter (:71, :236-243); one ticket is one (item, KV split)
+//     unit, so a long context is spread over several CTAs and merged afterwards;
+//   * loads: one producer warp streams K (16 B/key) and V (D B/key) pages through
+//     the TMA engine (cp.async.bulk + mbarrier complete_tx) into an NS-stage ring,
+//     replacing the cp.async 16 B copies and the 6-stage ring (:377-452);
+//   * per page, the block table gives the pool block (:402-411); a page id outside
+//     the pool raises HYPERION_DEVERR_BAD_BLOCK and its keys are skipped;
+//   * consumers: 4 warps, each owning a quarter of every stage's keys with its own
+//     running (m, l, acc); the score is D - 2*popcount(q XOR k) (README.md:22),
+//     the softmax the reference's clamped online update (:544-572) applied per
+//     16-key group, and the FP8 decode the reference's rule (:122-141) as bit moves;
+//   * the four per-warp states are merged through shared memory, then either
+//     finalised (:582-593) or written as a split-KV partial for the combine kernel.
+#pragma once
+
+#include "common.cuh"
+
+namespace hyp {
+namespace row {
+
+constexpr int kKeysPerStage = 64;
+constexpr int kStages = 4;
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = 32 * (1 + kConsumerWarps);
+constexpr int kKeysPerWarp = kKeysPerStage / kConsumerWarps;  // 16
+
+struct StageHeader {
+  int nkeys;
+  int pad;
+  unsigned long long mask;  // bit j: key j of the stage is present
+};
+
+struct UnitSlot {
+  int unit;   // -1: no more work
+  int item;
+  int bh;
+  int q_idx;
+  int k_lo;
+  int k_hi;
+  int valid;
+  int split;
+};
+
+template <int D>
+struct Smem {
+  static constexpr int W = D / 32;
+  static constexpr int kKBytes = kKeysPerStage * W * 4;
+  static constexpr int kVBytes = kKeysPerStage * D;
+  alignas(128) uint8_t k[kStages][kKBytes];
+  alignas(128) uint8_t v[kStages][kVBytes];
+  StageHeader hdr[kStages];
+  UnitSlot slot[2];
+  float merge_m[kConsumerWarps];
+  float merge_l[kConsumerWarps];
+  float merge_acc[kConsumerWarps][D];
+  alignas(8) uint64_t full[kStages];
+  alignas(8) uint64_t empty[kStages];
+  alignas(8) uint64_t unit_full[2];
+  alignas(8) uint64_t unit_empty[2];
+  int abort;
+};
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Loads this lane's D/32 V bytes of one stage row (lane owns dims [lane*D/32, +D/32)).
+template <int D>
+__device__ __forceinline__ void load_v_lane(const uint8_t* row, int lane, uint32_t (&w)[(D / 32 + 3) / 4]) {
+  if constexpr (D == 64) {
+    w[0] = *reinterpret_cast<const uint16_t*>(row + lane * 2);
+  } else if constexpr (D == 128) {
+    w[0] = *reinterpret_cast<const uint32_t*>(row + lane * 4);
+  } else {
+    const uint2 t = *reinterpret_cast<const uint2*>(row + lane * 8);
+    w[0] = t.x;
+    w[1] = t.y;
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 5) row_fwd_kernel(FwdParams p, int total_units) {
+  constexpr int W = D / 32;
+  constexpr int DPL = D / 32;  // dims per lane
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  Smem<D>& sm = *reinterpret_cast<Smem<D>*>(smem_raw);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], kConsumerWarps);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.unit_full[s], 1);
+      mbar_init(&sm.unit_empty[s], kConsumerWarps);
+    }
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  volatile int* abort = &sm.abort;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    const uint64_t pol = policy_evict_first();
+    uint32_t it = 0;
+    uint32_t ucount = 0;
+    for (;;) {
+      int t = 0;
+      if (lane == 0) t = (int)atomicAdd(&p.counters[0], 1u);
+      t = __shfl_sync(0xffffffffu, t, 0);
+      const int unit = (t < total_units) ? t : -1;
+      const int us = ucount & 1;
+      if (!mbar_wait(&sm.unit_empty[us], ((ucount >> 1) & 1) ^ 1, abort, p.err)) break;
+      int item = 0, split = 0, k_lo = 0, k_hi = 0, bh = 0, q_idx = 0;
+      bool valid = false;
+      if (unit >= 0) {
+        item = unit / p.n_split;
+        split = unit - item * p.n_split;
+        const ItemInfo inf = resolve_item(p, item);
+        bh = inf.bh;
+        q_idx = inf.q_idx;
+        valid = inf.valid;
+        if (valid) {
+          int chunk = (inf.kv_end + p.n_split - 1) / p.n_split;
+          chunk = (chunk + 15) & ~15;
+          k_lo = min(split * chunk, inf.kv_end);
+          k_hi = min(k_lo + chunk, inf.kv_end);
+        }
+        if (lane == 0 && split == 0) check_item_errors(p, item);
+      }
+      if (lane == 0) {
+        UnitSlot& sl = sm.slot[us];
+        sl.unit = unit;
+        sl.item = item;
+        sl.bh = bh;
+        sl.q_idx = q_idx;
+        sl.k_lo = k_lo;
+        sl.k_hi = k_hi;
+        sl.valid = valid ? 1 : 0;
+        sl.split = split;
+        mbar_arrive(&sm.unit_full[us]);
+      }
+      ++ucount;
+      if (unit < 0) break;
+
+      bool aborted = false;
+      for (int k0 = k_lo; k0 < k_hi; k0 += kKeysPerStage) {
+        const int s = it % kStages;
+        if (!mbar_wait(&sm.empty[s], ((it / kStages) & 1) ^ 1, abort, p.err)) {
+          aborted = true;
+          break;
+        }
+        const int n = min(kKeysPerStage, k_hi - k0);
+        const int bs = p.block_size;
+        const int p0 = k0 / bs;
+        const int np = (k0 + n - 1) / bs - p0 + 1;
+        uint32_t bytes = 0;
+        unsigned long long mask = 0ull;
+        for (int i = lane; i < np; i += 32) {
+          const int page = p0 + i;
+          const int lo = max(k0, page * bs);
+          const int hi = min(k0 + n, (page + 1) * bs);
+          const long long id = page_block_id(p, bh, page);
+          if (id >= 0) {
+            bytes += (uint32_t)(hi - lo) * (uint32_t)(W * 4 + D);
+            const int a = lo - k0, b = hi - k0;
+            const unsigned long long bits = (b - a >= 64) ? ~0ull : ((1ull << (b - a)) - 1ull);
+            mask |= bits << a;
+          } else {
+            raise_error(p.err, HYPERION_DEVERR_BAD_BLOCK);
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
+          mask |= __shfl_xor_sync(0xffffffffu, mask, o);
+        }
+        if (lane == 0) {
+          sm.hdr[s].nkeys = n;
+          sm.hdr[s].mask = mask;
+          if (bytes) {
+            mbar_arrive_expect_tx(&sm.full[s], bytes);
+          } else {
+            mbar_arrive(&sm.full[s]);
+          }
+        }
+        __syncwarp();
+        for (int i = lane; i < np; i += 32) {
+          const int page = p0 + i;
+          const int lo = max(k0, page * bs);
+          const int hi = min(k0 + n, (page + 1) * bs);
+          const long long id = page_block_id(p, bh, page);
+          if (id >= 0) {
+            const long long slot0 = id * bs + (lo - page * bs);
+            const uint32_t cnt = (uint32_t)(hi - lo);
+            bulk_g2s_stream(&sm.k[s][(lo - k0) * W * 4], p.k + slot0 * W, cnt * W * 4, &sm.full[s], pol);
+            bulk_g2s_stream(&sm.v[s][(lo - k0) * D], p.v + slot0 * D, cnt * D, &sm.full[s], pol);
+          }
+        }
+        ++it;
+      }
+      if (aborted) break;
+    }
+    if (*abort && lane == 0) {
+      // Let the copies of the last (up to kStages) armed stages land before exit.
+      for (uint32_t i = (it > (uint32_t)kStages ? it - kStages : 0u); i < it; ++i)
+        mbar_drain(&sm.full[i % kStages], (i / kStages) & 1);
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int cw = warp - 1;
+    uint32_t it = 0;
+    uint32_t ucount = 0;
+    for (;;) {
+      const int us = ucount & 1;
+      if (!mbar_wait(&sm.unit_full[us], (ucount >> 1) & 1, abort, p.err)) break;
+      const UnitSlot sl = sm.slot[us];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.unit_empty[us]);
+      ++ucount;
+      if (sl.unit < 0) break;
+
+      uint32_t q[W];
+      if (sl.valid) {
+        const uint32_t* qrow = p.q + ((long long)sl.bh * p.seq_q + sl.q_idx) * W;
+#pragma unroll
+        for (int i = 0; i < W; ++i) q[i] = __ldg(qrow + i);
+      } else {
+#pragma unroll
+        for (int i = 0; i < W; ++i) q[i] = 0u;
+      }
+      float m = -INFINITY, l = 0.f;
+      float acc[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+
+      bool aborted = false;
+      for (int k0 = sl.k_lo; k0 < sl.k_hi; k0 += kKeysPerStage) {
+        const int s = it % kStages;
+        if (!mbar_wait(&sm.full[s], (it / kStages) & 1, abort, p.err)) {
+          aborted = true;
+          break;
+        }
+        const int n = sm.hdr[s].nkeys;
+        const unsigned long long mask = sm.hdr[s].mask;
+        const int jl = cw * kKeysPerWarp + (lane & 15);
+        const bool ok = (lane < 16) && (jl < n) && ((mask >> jl) & 1ull);
+        float sc = -INFINITY;
+        if (ok) {
+          const uint32_t* kr = reinterpret_cast<const uint32_t*>(&sm.k[s][jl * W * 4]);
+          const int si = sign_score<W>(q, kr);
+          sc = (float)si * p.inv_sqrt_d;
+          if (p.debug_scores) p.debug_scores[(long long)sl.item * p.debug_ld + (k0 + jl)] = si;
+        }
+        const float mt = warp_max(sc);
+        if (mt != -INFINITY) {
+          const float m_new = fmaxf(m, mt);
+          const float alpha = (m == -INFINITY) ? 0.f : exp_clamped(m - m_new);
+          float w = ok ? exp_clamped(sc - m_new) : 0.f;
+          l = l * alpha + warp_sum(w);
+          if (p.v_scale_mode == 2 && ok) {
+            const int key = k0 + jl;
+            const int page = key / p.block_size;
+            const long long id = page_block_id(p, sl.bh, page);
+            w *= __ldg(p.v_scale + id * p.block_size + (key - page * p.block_size));
+          }
+          w *= kTwoPow120;
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) acc[i] *= alpha;
+          const uint8_t* vbase = &sm.v[s][(cw * kKeysPerWarp) * D];
+#pragma unroll 4
+          for (int jj = 0; jj < kKeysPerWarp; ++jj) {
+            const float wj = __shfl_sync(0xffffffffu, w, jj);
+            if (wj != 0.f) {
+              uint32_t vw[(DPL + 3) / 4];
+              load_v_lane<D>(vbase + jj * D, lane, vw);
+#pragma unroll
+              for (int i = 0; i < DPL; ++i) {
+                acc[i] = fmaf(wj, fp8_bits_to_f32_scaled(vw[i >> 2] >> (8 * (i & 3))), acc[i]);
+              }
+            }
+          }
+          m = m_new;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.empty[s]);
+        ++it;
+      }
+      // Every consumer warp reaches both named barriers below once per unit, also
+      // when it gave up on a wait: the barriers have no timeout of their own.
+      const bool stop = aborted || (*abort != 0);
+
+      // ---- merge the four warps' (m, l, acc) ----
+      if (lane == 0) {
+        sm.merge_m[cw] = m;
+        sm.merge_l[cw] = l;
+      }
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) sm.merge_acc[cw][lane * DPL + i] = acc[i];
+      named_bar_sync(1, 32 * kConsumerWarps);
+      float M = -INFINITY;
+#pragma unroll
+      for (int w2 = 0; w2 < kConsumerWarps; ++w2) M = fmaxf(M, sm.merge_m[w2]);
+      float f[kConsumerWarps];
+      float L = 0.f;
+#pragma unroll
+      for (int w2 = 0; w2 < kConsumerWarps; ++w2) {
+        const float mw = sm.merge_m[w2];
+        f[w2] = (mw == -INFINITY) ? 0.f : exp_clamped(mw - M);
+        L += sm.merge_l[w2] * f[w2];
+      }
+      const float vs_unit = (p.v_scale_mode == 2) ? 1.f : v_scale_for(p, sl.bh, 0);
+      for (int d = cw * 32 + lane; d < D; d += 32 * kConsumerWarps) {
+        float a = 0.f;
+#pragma unroll
+        for (int w2 = 0; w2 < kConsumerWarps; ++w2) a += sm.merge_acc[w2][d] * f[w2];
+        a *= vs_unit;
+        if (stop) continue;
+        if (p.n_split == 1) {
+          if (sl.valid) {
+            const float inv_l = (L > 1e-6f) ? 1.f / L : 1.f;
+            store_out(p.o, p.o_dtype, ((long long)sl.bh * p.seq_q + sl.q_idx) * D + d, a * inv_l);
+          }
+        } else {
+          float* part = p.partials + (long long)sl.unit * (2 + D);
+          part[2 + d] = a;
+          if (d == 0) {
+            part[0] = M;
+            part[1] = L;
+          }
+        }
+      }
+      named_bar_sync(1, 32 * kConsumerWarps);
+      if (stop) break;
+    }
+  }
+}
+
+// Merges the n_split partials (m, l, acc[D]) of every item and writes O.
+template <int D>
+__global__ void __launch_bounds__(128) row_combine_kernel(FwdParams p) {
+  const int item = blockIdx.x;
+  const ItemInfo inf = resolve_item(p, item);
+  if (!inf.valid) return;
+  const float* base = p.partials + (long long)item * p.n_split * (2 + D);
+  float M = -INFINITY;
+  for (int s = 0; s < p.n_split; ++s) M = fmaxf(M, base[s * (2 + D)]);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float L = 0.f, a = 0.f;
+    for (int s = 0; s < p.n_split; ++s) {
+      const float* part = base + s * (2 + D);
+      const float ms = part[0];
+      const float f = (ms == -INFINITY) ? 0.f : exp_clamped(ms - M);
+      L += part[1] * f;
+      a += part[2 + d] * f;
+    }
+    const float inv_l = (L > 1e-6f) ? 1.f / L : 1.f;
+    store_out(p.o, p.o_dtype, ((long long)inf.bh * p.seq_q + inf.q_idx) * D + d, a * inv_l);
+  }
+}
+
+}  // namespace row
+}  // namespace hyp

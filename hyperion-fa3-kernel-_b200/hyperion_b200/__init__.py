@@ -1,0 +1,234 @@
+"""B200 (sm_100a) drop-in for the reference's `hyperion` extension module.
+
+The reference builds its forward with `load_inline` and uses the module object
+as `hyperion` (hyperion_fa3_production_final.py:613-634):
+
+    hyperion.hyperion_reset_counter(grid=(1, 1, 1), block=(1, 1, 1))          # :905
+    hyperion.hyperion_apex_kernel(worklist, n, Q, Q_scale, K, K_scale, V, V_scale,
+        ctx_lens, block_tables, O, seq_q, D, k_packed_bytes, block_size,
+        num_blocks, inv_sqrt_d, causal, grid=grid, block=block, shared=smem)  # :1099-1114
+
+This package exposes the same two names with the same argument order and
+meaning, so a caller swaps the module object and nothing else:
+
+    import hyperion_b200 as hyperion
+    HYPERION_LOADED = hyperion.HYPERION_LOADED
+
+Tensors are torch CUDA tensors (PyTorch is plumbing here: device memory and the
+current stream); every call goes through the C ABI of libhyperion_b200.so.
+Differences from the reference's boundary, all forced by the sign-bit path:
+  * Q and K_cache hold sign bits packed into uint32 words (int32 / uint32 / uint8
+    storage of the same bytes); k_packed_bytes must be head_dim // 8;
+  * Q_scale and K_scale are accepted and ignored;
+  * V_scale may be per tensor (numel 1), per slot (numel == pool rows) or per
+    head / per (batch, head) (index bh % numel);
+  * O may be float16 (the reference's type), bfloat16 or float32;
+  * grid / block / shared are accepted as hints: the library sizes its own launch;
+  * a block_tables tensor with numel 0 selects the contiguous KV layout.
+Errors in arguments raise RuntimeError (the reference's TORCH_CHECK would);
+errors found on the device (bad block ids, out-of-range work items) are
+accumulated in a per-device error word: `read_device_errors()`.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from typing import Optional
+
+import torch
+
+from . import _capi
+from ._capi import (  # noqa: F401
+    DEVERR_BAD_BLOCK,
+    DEVERR_BAD_ITEM,
+    DEVERR_CTX_OVERFLOW,
+    DEVERR_NEG_CTX,
+    DEVERR_WAIT_TIMEOUT,
+    PATH_AUTO,
+    PATH_ROW,
+    PATH_TILE,
+)
+
+HYPERION_LOADED = True
+__version__ = "1.0.0"
+
+_O_DTYPES = {torch.float16: _capi.DTYPE_F16, torch.bfloat16: _capi.DTYPE_BF16, torch.float32: _capi.DTYPE_F32}
+_PATHS = {"auto": _capi.PATH_AUTO, "row": _capi.PATH_ROW, "tile": _capi.PATH_TILE}
+
+_ws_lock = threading.Lock()
+_workspaces: dict = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Per-device workspace (work counter, error word, split-KV partials), grown on demand."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with _ws_lock:
+        ws = _workspaces.get(idx)
+        if ws is None or ws.numel() < nbytes:
+            new = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=torch.device("cuda", idx))
+            if ws is not None:
+                new[:256].copy_(ws[:256])  # keep the sticky error word
+            ws = new
+            _workspaces[idx] = ws
+        return ws
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None or t.numel() == 0 else t.data_ptr()
+
+
+def _check(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(f"hyperion_apex_kernel: {msg}")
+
+
+def _nbytes(t: torch.Tensor) -> int:
+    return t.numel() * t.element_size()
+
+
+def hyperion_apex_kernel(
+    worklist: torch.Tensor,
+    total_work: int,
+    Q: torch.Tensor,
+    Q_scale: Optional[torch.Tensor],
+    K_cache: torch.Tensor,
+    K_scale: Optional[torch.Tensor],
+    V_cache: torch.Tensor,
+    V_scale: torch.Tensor,
+    context_lens: torch.Tensor,
+    block_tables: Optional[torch.Tensor],
+    O: torch.Tensor,
+    seq_q: int,
+    head_dim: int,
+    k_packed_bytes: int,
+    block_size: int,
+    num_blocks: int,
+    inv_sqrt_d: float,
+    causal: bool,
+    *,
+    grid=None,
+    block=None,
+    shared=None,
+    path: str = "auto",
+    num_splits: int = 0,
+    debug_scores: Optional[torch.Tensor] = None,
+) -> None:
+    """Enqueues the forward on the current CUDA stream of O's device (asynchronous).
+
+    Same positional signature as the reference's kernel entry
+    (hyperion_fa3_production_final.py:268-288).  `path`, `num_splits` and
+    `debug_scores` (int32 [total_work, L]: receives head_dim - 2*popcount for
+    every attended key) are extensions for tests and tuning.
+    """
+    total_work = int(total_work)
+    _check(O.is_cuda, "O must be a CUDA tensor")
+    dev = O.device
+    for name, t in (("worklist", worklist), ("Q", Q), ("K_cache", K_cache), ("V_cache", V_cache),
+                    ("V_scale", V_scale), ("context_lens", context_lens)):
+        _check(t.is_cuda and t.device == dev, f"{name} must be on {dev}")
+        _check(t.is_contiguous(), f"{name} must be contiguous")
+    _check(worklist.dtype == torch.int32 and worklist.dim() == 2 and worklist.size(1) == 4,
+           "worklist must be int32 [n, 4]")
+    _check(0 <= total_work <= worklist.size(0), "total_work must be in [0, worklist.size(0)]")
+    _check(context_lens.dtype == torch.int32, "context_lens must be int32")
+    _check(V_scale.dtype == torch.float32 and V_scale.numel() >= 1, "V_scale must be a non-empty float32 tensor")
+    _check(V_cache.element_size() == 1, "V_cache must hold one byte per element (FP8 e4m3 codes)")
+    _check(O.dtype in _O_DTYPES, "O must be float16, bfloat16 or float32")
+    _check(O.is_contiguous(), "O must be contiguous")
+    _check(head_dim in (128, 256), "head_dim must be 128 or 256")
+    _check(k_packed_bytes == head_dim // 8, "k_packed_bytes must be head_dim // 8 (sign-bit K)")
+    n_bh = context_lens.numel()
+    row_bytes = head_dim // 8
+    _check(_nbytes(Q) >= n_bh * seq_q * row_bytes, "Q smaller than n_bh * seq_q rows of head_dim/8 bytes")
+    _check(_nbytes(K_cache) % row_bytes == 0, "K_cache bytes must be a multiple of head_dim/8")
+    _check(V_cache.numel() % head_dim == 0, "V_cache numel must be a multiple of head_dim")
+    pool_rows = min(_nbytes(K_cache) // row_bytes, V_cache.numel() // head_dim)
+    _check(O.numel() >= n_bh * seq_q * head_dim, "O smaller than n_bh * seq_q * head_dim")
+    bt_numel = 0
+    if block_tables is not None and block_tables.numel() > 0:
+        _check(block_tables.is_cuda and block_tables.device == dev and block_tables.is_contiguous(),
+               "block_tables must be a contiguous CUDA tensor on O's device")
+        _check(block_tables.dtype == torch.int32, "block_tables must be int32")
+        bt_numel = block_tables.numel()
+        _check(bt_numel >= n_bh * num_blocks, "block_tables numel < n_bh * num_blocks")
+    if debug_scores is not None:
+        _check(debug_scores.is_cuda and debug_scores.dtype == torch.int32 and debug_scores.dim() == 2
+               and debug_scores.is_contiguous() and debug_scores.size(0) >= total_work,
+               "debug_scores must be a contiguous int32 CUDA tensor [>= total_work, L]")
+    _check(path in _PATHS, f"path must be one of {sorted(_PATHS)}")
+
+    def _hint(x, i=0):
+        if x is None:
+            return 0
+        if isinstance(x, (tuple, list)):
+            return int(x[i]) if len(x) > i else 0
+        return int(x)
+
+    ext = _capi.Extents(n_bh, pool_rows, V_scale.numel(), bt_numel, _O_DTYPES[O.dtype],
+                        _hint(grid), _hint(block), _hint(shared))
+    opt = _capi.Options(_PATHS[path], int(num_splits),
+                        debug_scores.data_ptr() if debug_scores is not None else None,
+                        debug_scores.size(1) if debug_scores is not None else 0)
+    with torch.cuda.device(dev):
+        need = _capi.lib.hyperion_workspace_bytes(total_work, head_dim, block_size, num_blocks)
+        _check(need > 0, f"hyperion_workspace_bytes failed: {_capi.last_error()}")
+        ws = _workspace(dev, need)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = _capi.lib.hyperion_apex_kernel_ex(
+            _ptr(worklist), total_work, _ptr(Q), _ptr(Q_scale), _ptr(K_cache), _ptr(K_scale),
+            _ptr(V_cache), _ptr(V_scale), _ptr(context_lens),
+            block_tables.data_ptr() if bt_numel else None, _ptr(O),
+            int(seq_q), int(head_dim), int(k_packed_bytes), int(block_size), int(num_blocks),
+            float(inv_sqrt_d), 1 if causal else 0, ctypes.byref(ext), ctypes.byref(opt),
+            ws.data_ptr(), ws.numel(), stream)
+    if rc != _capi.HYPERION_OK:
+        raise RuntimeError(f"hyperion_apex_kernel failed (status {rc}): {_capi.last_error()}")
+
+
+def hyperion_reset_counter(*, grid=None, block=None, device=None) -> None:
+    """Reference call site hyperion_fa3_production_final.py:905.  Zeroes the work
+    counter of the current device's workspace on the current stream.  The forward
+    also zeroes it itself, so calling this is optional."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index)
+    with torch.cuda.device(dev):
+        ws = _workspace(dev, 1 << 16)
+        rc = _capi.lib.hyperion_reset_counter(ws.data_ptr(), ws.numel(), torch.cuda.current_stream(dev).cuda_stream)
+    if rc != _capi.HYPERION_OK:
+        raise RuntimeError(f"hyperion_reset_counter failed (status {rc}): {_capi.last_error()}")
+
+
+def read_device_errors(device=None, clear: bool = True) -> int:
+    """Synchronises the current stream and returns the DEVERR_* flags raised on `device`."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index)
+    with torch.cuda.device(dev):
+        ws = _workspace(dev, 1 << 16)
+        flags = ctypes.c_uint32(0)
+        rc = _capi.lib.hyperion_read_device_errors(ws.data_ptr(), ws.numel(), torch.cuda.current_stream(dev).cuda_stream,
+                                                   ctypes.byref(flags), 1 if clear else 0)
+    if rc != _capi.HYPERION_OK:
+        raise RuntimeError(f"hyperion_read_device_errors failed (status {rc}): {_capi.last_error()}")
+    return int(flags.value)
+
+
+def launch_info() -> dict:
+    """Launch facts derived from the current device (SM count, CTAs per SM, shared memory)."""
+    out = (ctypes.c_int32 * 7)()
+    rc = _capi.lib.hyperion_launch_info(out, 7)
+    if rc != _capi.HYPERION_OK:
+        raise RuntimeError(f"hyperion_launch_info failed: {_capi.last_error()}")
+    keys = ("sm_count", "row_ctas_per_sm", "row_smem_bytes", "tile_ctas_per_sm", "tile_smem_bytes",
+            "row_ctas_per_sm_d256", "tile_available")
+    return dict(zip(keys, list(out)))
+
+
+def last_call_info() -> dict:
+    """What the last forward on this thread launched: path ('row' / 'tile' / None),
+    KV splits per item, number of kernels and the main kernel's grid."""
+    out = (ctypes.c_int32 * 4)()
+    _capi.lib.hyperion_last_call_info(out, 4)
+    path = {_capi.PATH_ROW: "row", _capi.PATH_TILE: "tile"}.get(out[0])
+    return {"path": path, "splits": out[1], "kernels": out[2], "grid": out[3]}
+
+
+def library_path() -> str:
+    return _capi.LIB_PATH

@@ -1,0 +1,165 @@
+/*
+ * hyperion_b200.h -- C ABI of the B200 (sm_100a) sign-bit / FP8 attention forward.
+ *
+ * The reference project exposes its forward as a torch extension built by
+ * `load_inline` (hyperion_fa3_production_final.py:613-628) whose module object
+ * `hyperion` has two entry points:
+ *
+ *   hyperion.hyperion_apex_kernel(worklist, total_work, Q, Q_scale, K_cache, K_scale,
+ *        V_cache, V_scale, context_lens, block_tables, O, seq_q, head_dim,
+ *        k_packed_bytes, block_size, num_blocks, inv_sqrt_d, causal,
+ *        grid=, block=, shared=)          -- call site hyperion_fa3_production_final.py:1099-1114
+ *   hyperion.hyperion_reset_counter(grid=, block=)
+ *                                          -- call site hyperion_fa3_production_final.py:905
+ *
+ * The functions below are what an FFI (ctypes / cffi / pybind) binds in place of
+ * that module.  The positional arguments keep the reference's order and meaning;
+ * the sizes a raw pointer does not carry travel in `hyperion_extents`.  No torch
+ * type appears in any signature: tensors are plain device pointers, the stream is
+ * a cudaStream_t passed as void*.
+ *
+ * Data layout (device memory, caller-owned):
+ *   worklist      int32 [total_work, 4]  {q_idx, bh, kv_signature, prefetch_hint};
+ *                 only q_idx and bh are read (hyperion_fa3_production_final.py:248-253).
+ *   Q             uint32 [n_bh * seq_q, head_dim/32]  sign bits, bit d%32 of word d/32,
+ *                 bit = 1 where the value is >= 0.  Row (bh*seq_q + q_idx).
+ *   K_cache       uint32 [pool_rows, head_dim/32]  sign bits, same packing.
+ *   V_cache       uint8  [pool_rows, head_dim]     FP8 e4m3 codes, decoded with the
+ *                 reference's rule (bias 7, subnormals, exponent 15 finite:
+ *                 hyperion_fa3_production_final.py:122-141).
+ *   V_scale       float32, per tensor (numel 1), per slot (numel == pool_rows) or
+ *                 per head / per (batch, head) (index bh % numel).
+ *   context_lens  int32 [n_bh]   number of keys of each (batch, head).
+ *   block_tables  int32 [n_bh, num_blocks]  page ids; key t of bh lives in slot
+ *                 block_tables[bh*num_blocks + t/block_size]*block_size + t%block_size
+ *                 (hyperion_fa3_production_final.py:402-411).  A NULL table (or
+ *                 block_tables_numel == 0) means the contiguous layout
+ *                 slot = bh*num_blocks*block_size + t.
+ *   O             [n_bh * seq_q, head_dim] of f16, bf16 or f32 (ext->o_dtype).
+ *   Q_scale, K_scale are accepted and ignored: the reference ignores Q_scale, and
+ *   a sign-bit K has no magnitude.
+ *
+ * Math (per work item, q = Q row, keys t < context_lens[bh], and t <= q_idx when causal):
+ *   s_t = (head_dim - 2*popcount(q XOR k_t)) * inv_sqrt_d       (README.md:22)
+ *   online softmax with EXP_CLAMP = -80 (hyperion_fa3_production_final.py:544-547),
+ *   acc = sum_t w_t * fp8(v_t) * vscale, O = acc * (l > 1e-6 ? 1/l : 1)  (:582-593).
+ */
+#ifndef HYPERION_B200_H
+#define HYPERION_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Host-side status codes returned by every entry point. */
+#define HYPERION_OK                 0
+#define HYPERION_ERR_INVALID_ARG    1  /* a pointer, size or alignment check failed */
+#define HYPERION_ERR_UNSUPPORTED    2  /* a valid request this build does not implement */
+#define HYPERION_ERR_WORKSPACE      3  /* workspace missing or too small */
+#define HYPERION_ERR_CUDA           4  /* a CUDA runtime call failed */
+
+/* Device-side error flags, accumulated in the workspace error word and read back
+ * with hyperion_read_device_errors().  The kernels never trap: a bad input sets a
+ * flag and the offending key / item is skipped. */
+#define HYPERION_DEVERR_BAD_ITEM      0x1u  /* worklist bh or q_idx out of range: row not written */
+#define HYPERION_DEVERR_BAD_BLOCK     0x2u  /* block-table page id outside the page pool: keys skipped */
+#define HYPERION_DEVERR_CTX_OVERFLOW  0x4u  /* context_lens beyond num_blocks*block_size: tail skipped */
+#define HYPERION_DEVERR_NEG_CTX       0x8u  /* negative context length, treated as 0 */
+#define HYPERION_DEVERR_WAIT_TIMEOUT  0x10u /* a bounded device wait expired; output incomplete */
+
+/* Output element types for hyperion_extents.o_dtype. */
+#define HYPERION_DTYPE_F16   0
+#define HYPERION_DTYPE_BF16  1
+#define HYPERION_DTYPE_F32   2
+
+/* Kernel selection for hyperion_options.path. */
+#define HYPERION_PATH_AUTO   0  /* tile path when seq_q >= 64 and the inputs allow it, else row path */
+#define HYPERION_PATH_ROW    1  /* split-KV row kernel (CUDA cores, HBM streaming): any input */
+#define HYPERION_PATH_TILE   2  /* 128-row tcgen05 tile kernel: head_dim 128, non per-slot V scale */
+
+typedef struct hyperion_extents {
+  int32_t n_bh;               /* numel of context_lens: number of (batch, head) rows */
+  int64_t pool_rows;          /* rows of K_cache and of V_cache */
+  int64_t v_scale_numel;      /* numel of V_scale */
+  int64_t block_tables_numel; /* numel of block_tables; 0 selects the contiguous layout */
+  int32_t o_dtype;            /* HYPERION_DTYPE_* of O */
+  int32_t grid_hint;          /* the reference's grid= x (advisory, may be 0) */
+  int32_t block_hint;         /* the reference's block= x (advisory, may be 0) */
+  int32_t shared_hint;        /* the reference's shared= bytes (advisory, may be 0) */
+} hyperion_extents;
+
+typedef struct hyperion_options {
+  int32_t path;          /* HYPERION_PATH_* */
+  int32_t num_splits;    /* row path: KV splits per item, 0 = automatic */
+  int32_t* debug_scores; /* optional: int32 [total_work, debug_ld] receives the integer
+                            scores head_dim - 2*popcount for every key the item attends
+                            (masked keys are left untouched); NULL in production */
+  int64_t debug_ld;      /* row stride of debug_scores in elements */
+} hyperion_options;
+
+/* Bytes of device workspace the forward needs for these sizes (an upper bound). */
+size_t hyperion_workspace_bytes(int32_t total_work, int32_t head_dim,
+                                int32_t block_size, int32_t num_blocks);
+
+/* Replaces hyperion.hyperion_apex_kernel (hyperion_fa3_production_final.py:268-288
+ * signature, call site :1099-1114).  Asynchronous on `stream`; returns a host
+ * status after validating every size and pointer and enqueueing the kernels.
+ * `workspace` must be device memory of at least hyperion_workspace_bytes() bytes,
+ * 256-byte aligned; it holds the work counter, the error word and split-KV partials. */
+int hyperion_apex_kernel(const int32_t* worklist, int32_t total_work,
+                         const uint32_t* Q, const float* Q_scale,
+                         const uint32_t* K_cache, const float* K_scale,
+                         const uint8_t* V_cache, const float* V_scale,
+                         const int32_t* context_lens, const int32_t* block_tables,
+                         void* O, int32_t seq_q, int32_t head_dim, int32_t k_packed_bytes,
+                         int32_t block_size, int32_t num_blocks, float inv_sqrt_d,
+                         int32_t causal, const hyperion_extents* ext,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* The same forward with kernel selection and the debug score export. */
+int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work,
+                            const uint32_t* Q, const float* Q_scale,
+                            const uint32_t* K_cache, const float* K_scale,
+                            const uint8_t* V_cache, const float* V_scale,
+                            const int32_t* context_lens, const int32_t* block_tables,
+                            void* O, int32_t seq_q, int32_t head_dim, int32_t k_packed_bytes,
+                            int32_t block_size, int32_t num_blocks, float inv_sqrt_d,
+                            int32_t causal, const hyperion_extents* ext,
+                            const hyperion_options* opt,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+/* Replaces hyperion.hyperion_reset_counter (hyperion_fa3_production_final.py:73-77,
+ * call site :905).  The work counter lives in the caller's workspace instead of a
+ * __device__ global, so two streams never share it; the forward zeroes it itself
+ * on its own stream, and this call zeroes it explicitly (asynchronous on `stream`). */
+int hyperion_reset_counter(void* workspace, size_t workspace_bytes, void* stream);
+
+/* Synchronises `stream`, returns the accumulated HYPERION_DEVERR_* flags of this
+ * workspace in *flags and clears them when `clear` is non-zero. */
+int hyperion_read_device_errors(void* workspace, size_t workspace_bytes, void* stream,
+                                uint32_t* flags, int32_t clear);
+
+/* Launch facts the library derived from the device: SM count, CTAs per SM of the
+ * row kernel and of the tile kernel, and the dynamic shared memory of each.
+ * Fills up to `n` int32 values of `out`; returns HYPERION_OK. */
+int hyperion_launch_info(int32_t* out, int32_t n);
+
+/* What the last forward on this thread did: out[0] = path (HYPERION_PATH_ROW or
+ * _TILE, 0 when nothing was launched), out[1] = KV splits per item, out[2] = kernels
+ * launched, out[3] = grid size of the main kernel.  Fills up to `n` values. */
+int hyperion_last_call_info(int32_t* out, int32_t n);
+
+/* Last CUDA error string seen by the library on this thread ("" if none). */
+const char* hyperion_last_error_string(void);
+
+/* Library version as major*10000 + minor*100 + patch. */
+int32_t hyperion_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HYPERION_B200_H */

@@ -1,0 +1,74 @@
+"""The C-ABI library loads without a GPU and exports every symbol its header
+declares; the Python drop-in keeps the reference's entry names and rejects bad
+arguments before touching a device."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "hyperion_b200.h")
+
+
+def _declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    names = re.findall(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\*?\s*(hyperion_[a-z_]+)\s*\(", src, flags=re.M)
+    return sorted(set(names))
+
+
+def test_header_declares_the_expected_entry_points():
+    names = _declared_functions()
+    assert "hyperion_apex_kernel" in names and "hyperion_reset_counter" in names
+    from hyperion_b200 import _capi
+
+    assert set(names) == set(_capi.EXPORTED)
+
+
+def test_library_loads_and_exports_every_declared_symbol(hyperion):
+    lib = ctypes.CDLL(hyperion.library_path())
+    for name in _declared_functions():
+        assert hasattr(lib, name), name
+    assert lib.hyperion_version() == 10000
+
+
+def test_drop_in_names_match_reference_module(hyperion):
+    # hyperion_fa3_production_final.py:598-601 binds exactly these two names.
+    assert callable(hyperion.hyperion_apex_kernel)
+    assert callable(hyperion.hyperion_reset_counter)
+    assert hyperion.HYPERION_LOADED is True
+
+
+def test_python_boundary_rejects_cpu_tensors(hyperion):
+    t = torch.zeros(4, 4, dtype=torch.int32)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        hyperion.hyperion_apex_kernel(t, 4, t, None, t, None, t.to(torch.uint8), torch.ones(1), t[0],
+                                      None, torch.zeros(4, 128), 1, 128, 16, 16, 1, 0.088, False)
+
+
+def test_c_boundary_rejects_bad_sizes_without_touching_the_device(hyperion):
+    from hyperion_b200 import _capi
+
+    lib = _capi.lib
+    ext = _capi.Extents(1, 16, 1, 0, _capi.DTYPE_F32, 0, 0, 0)
+    fake = ctypes.c_void_p(256)
+    args = [fake, 1, fake, None, fake, None, fake, fake, fake, None, fake, 1, 128, 64, 16, 1,
+            ctypes.c_float(0.088), 0, ctypes.byref(ext), fake, 1 << 20, None]
+    # k_packed_bytes 64 is the reference's INT4 value; sign-bit K needs head_dim/8.
+    assert lib.hyperion_apex_kernel(*args) == _capi.HYPERION_ERR_INVALID_ARG
+    assert "k_packed_bytes" in _capi.last_error()
+    args[13] = 16
+    args[12] = 96
+    assert lib.hyperion_apex_kernel(*args) == _capi.HYPERION_ERR_UNSUPPORTED
+    args[12] = 128
+    args[11] = 0  # seq_q
+    assert lib.hyperion_apex_kernel(*args) == _capi.HYPERION_ERR_INVALID_ARG
+    args[11] = 1
+    args[19] = None  # workspace
+    assert lib.hyperion_apex_kernel(*args) == _capi.HYPERION_ERR_WORKSPACE
+    ext_bad = _capi.Extents(1, 16, 1, 5, _capi.DTYPE_F32, 0, 0, 0)  # table numel without pointer
+    args[19] = fake
+    args[18] = ctypes.byref(ext_bad)
+    assert lib.hyperion_apex_kernel(*args) == _capi.HYPERION_ERR_INVALID_ARG

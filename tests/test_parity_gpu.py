@@ -1,0 +1,236 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle.
+
+Bar (the reference's own tolerance for this path): integer QK scores bit-exact;
+outputs within max-abs 2e-2 and mean-abs 2e-3 of the oracle in fp32.  Every test
+here is marked gpu; none of them makes a GPU fault or hang: bad inputs are
+host-built and the kernels turn them into error flags.
+"""
+import numpy as np
+import pytest
+import torch
+
+from hyperion_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+MEAN_ABS = 2e-3
+
+
+def run(hyperion, wk, path="auto", num_splits=0, debug_ld=0, o_dtype=None):
+    dev = torch.device("cuda", 0)
+    g = wk.to(dev)
+    o = torch.full((g.n_bh * g.seq_q, g.head_dim), float("nan"), dtype=o_dtype or g.o_dtype, device=dev)
+    dbg = torch.zeros(g.total_work, debug_ld, dtype=torch.int32, device=dev) if debug_ld else None
+    hyperion.read_device_errors(dev, clear=True)
+    hyperion.hyperion_apex_kernel(g.worklist, g.total_work, g.q, None, g.k, None, g.v, g.v_scale, g.ctx_lens,
+                                  g.block_tables, o, g.seq_q, g.head_dim, g.head_dim // 8, g.block_size,
+                                  g.num_blocks, g.inv_sqrt_d, g.causal, path=path, num_splits=num_splits,
+                                  debug_scores=dbg)
+    err = hyperion.read_device_errors(dev, clear=True)
+    return o.float().cpu().numpy(), err, (dbg.cpu().numpy() if dbg is not None else None)
+
+
+def check(oracle, wk, o_gpu, rows=None):
+    o_ref, written, err, _ = oracle.forward_workload_c(wk)
+    if rows is not None:
+        o_ref, o_gpu = o_ref[rows], o_gpu[rows]
+    ok, mx, mn = oracle.tolerance_check(o_gpu, o_ref, MAX_ABS, MEAN_ABS)
+    assert ok, f"max {mx:.3e} mean {mn:.3e}"
+    return mx, mn
+
+
+def written_rows(wk):
+    wl = wk.worklist.cpu().numpy()
+    return (wl[:, 1].astype(np.int64) * wk.seq_q + wl[:, 0]).tolist()
+
+
+# ----------------------------------------------------------------------------- row path
+@pytest.mark.parametrize("o_dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_cpu_ref_config_row_path(hyperion, oracle, o_dtype):
+    wk = W.make_config("cpu_ref", device="cpu", exact=True)
+    o, err, _ = run(hyperion, wk, path="row", o_dtype=o_dtype)
+    assert err == 0
+    check(oracle, wk, o)
+
+
+@pytest.mark.parametrize("num_splits", [1, 3, 7, 16])
+def test_row_path_split_kv(hyperion, oracle, num_splits):
+    wk = W.make_dense("d", 2, 4, 1, 3000, scale_mode="head", o_dtype=torch.float32, seed=3)
+    o, err, _ = run(hyperion, wk, path="row", num_splits=num_splits)
+    assert err == 0
+    check(oracle, wk, o)
+
+
+@pytest.mark.parametrize("scale_mode", ["tensor", "head", "bh"])
+def test_row_path_causal_ragged_prefill(hyperion, oracle, scale_mode):
+    wk = W.make_dense("c", 2, 3, 157, 157, causal=True, scale_mode=scale_mode, o_dtype=torch.float32, seed=5)
+    o, err, _ = run(hyperion, wk, path="row")
+    assert err == 0
+    check(oracle, wk, o)
+
+
+def test_row_path_paged_decode_ragged(hyperion, oracle):
+    lens = [1, 15, 16, 17, 100, 511, 2000, 4097]
+    wk = W.make_paged("p", len(lens), 4, lens, page=16, seed=6, o_dtype=torch.float32)
+    o, err, _ = run(hyperion, wk, path="row")
+    assert err == 0
+    check(oracle, wk, o)
+
+
+@pytest.mark.parametrize("page", [1, 8, 64, 256])
+def test_row_path_page_sizes(hyperion, oracle, page):
+    wk = W.make_paged("p", 3, 2, [300, 77, 1000], page=page, seed=8, o_dtype=torch.float32)
+    o, err, _ = run(hyperion, wk, path="row")
+    assert err == 0
+    check(oracle, wk, o)
+
+
+def test_row_path_per_slot_scale(hyperion, oracle):
+    wk = W.make_paged("p", 2, 2, [200, 333], page=16, seed=9, o_dtype=torch.float32)
+    pool_rows = wk.v.shape[0]
+    g = torch.Generator().manual_seed(1)
+    wk.v_scale = (torch.rand(pool_rows, generator=g) * 0.02 + 0.001).to(torch.float32)
+    o, err, _ = run(hyperion, wk, path="row")
+    assert err == 0
+    check(oracle, wk, o)
+
+
+def test_row_path_head_dim_256(hyperion, oracle):
+    wk = W.make_dense("d256", 1, 3, 5, 700, D=256, causal=True, scale_mode="head", o_dtype=torch.float32, seed=12)
+    o, err, _ = run(hyperion, wk, path="row")
+    assert err == 0
+    check(oracle, wk, o)
+
+
+def test_row_path_scores_bit_exact(hyperion, oracle):
+    wk = W.make_paged("p", 3, 2, [50, 129, 700], page=16, seed=13, o_dtype=torch.float32)
+    L = 700
+    _, _, _, sc_ref = oracle.forward_workload_c(wk, scores_ld=L)
+    _, err, sc = run(hyperion, wk, path="row", debug_ld=L)
+    assert err == 0
+    assert np.array_equal(sc, sc_ref)
+
+
+def test_row_path_fully_masked_rows_are_zero(hyperion, oracle):
+    wk = W.make_dense("m", 1, 4, 1, 64, o_dtype=torch.float32, seed=14)
+    wk.ctx_lens[1] = 0
+    wk.ctx_lens[3] = 0
+    o, err, _ = run(hyperion, wk, path="row", num_splits=2)
+    assert err == 0
+    assert np.all(o[1] == 0) and np.all(o[3] == 0)
+    check(oracle, wk, o)
+
+
+def test_row_path_bad_block_and_item_raise_flags(hyperion, oracle):
+    wk = W.make_paged("p", 2, 2, [64, 64], page=16, seed=15, o_dtype=torch.float32)
+    wk.block_tables[1, 2] = 1 << 30
+    wk.block_tables[2, 0] = -7
+    wl = wk.worklist.clone()
+    wl[3, 1] = 1000
+    wk.worklist = wl
+    o, err, _ = run(hyperion, wk, path="row")
+    assert err & hyperion.DEVERR_BAD_BLOCK and err & hyperion.DEVERR_BAD_ITEM
+    assert np.isnan(o[3]).all()  # the out-of-range item's row is never written
+    check(oracle, wk, o, rows=[0, 1, 2])
+
+
+def test_row_path_context_overflow_flag(hyperion, oracle):
+    wk = W.make_dense("o", 1, 2, 1, 128, o_dtype=torch.float32, seed=16)
+    wk.ctx_lens[0] = 5000  # beyond num_blocks * block_size = 128
+    o, err, _ = run(hyperion, wk, path="row")
+    assert err & hyperion.DEVERR_CTX_OVERFLOW
+    check(oracle, wk, o)
+
+
+def test_empty_worklist_is_a_no_op(hyperion):
+    dev = torch.device("cuda", 0)
+    wl = torch.zeros(0, 4, dtype=torch.int32, device=dev)
+    o = torch.full((4, 128), 7.0, device=dev)
+    z = torch.zeros(4, 4, dtype=torch.int32, device=dev)
+    hyperion.hyperion_apex_kernel(wl, 0, z, None, z, None, torch.zeros(4, 128, dtype=torch.uint8, device=dev),
+                                  torch.ones(1, device=dev), torch.ones(1, dtype=torch.int32, device=dev), None, o,
+                                  4, 128, 16, 4, 1, 0.088, False)
+    torch.cuda.synchronize()
+    assert torch.all(o == 7.0)
+
+
+def test_reset_counter_and_repeat_calls_are_stable(hyperion, oracle):
+    wk = W.make_dense("r", 2, 2, 1, 999, o_dtype=torch.float32, seed=17)
+    o1, _, _ = run(hyperion, wk, path="row")
+    hyperion.hyperion_reset_counter(grid=(1, 1, 1), block=(1, 1, 1))
+    o2, _, _ = run(hyperion, wk, path="row")
+    assert np.array_equal(o1, o2)
+
+
+# ----------------------------------------------------------------------------- full-size, sampled rows
+def _sampled_check(hyperion, oracle, name, n_rows=24, path="auto"):
+    dev = torch.device("cuda", 0)
+    wk = W.make_config(name, device=dev, exact=False)
+    o = wk.new_output()
+    hyperion.read_device_errors(dev, clear=True)
+    hyperion.hyperion_apex_kernel(wk.worklist, wk.total_work, wk.q, None, wk.k, None, wk.v, wk.v_scale,
+                                  wk.ctx_lens, wk.block_tables, o, wk.seq_q, wk.head_dim, wk.head_dim // 8,
+                                  wk.block_size, wk.num_blocks, wk.inv_sqrt_d, wk.causal, path=path)
+    assert hyperion.read_device_errors(dev, clear=True) == 0
+    assert torch.isfinite(o.float()).all()
+    g = torch.Generator().manual_seed(0)
+    items = torch.randperm(wk.total_work, generator=g)[:n_rows].sort().values.tolist()
+    sub, rows = compact_subset(wk, items)
+    o_ref, _, _, _ = oracle.forward_workload_c(sub)
+    ok, mx, mn = oracle.tolerance_check(o.float().cpu().numpy()[rows], o_ref, MAX_ABS, MEAN_ABS)
+    assert ok, (mx, mn)
+
+
+def compact_subset(wk, items):
+    """The keys the listed work items attend, gathered on the device into a small
+    contiguous CPU workload (one bh per item, non-causal with the causal bound
+    folded into its length).  Returns (workload, output rows of the items in wk)."""
+    wl = wk.worklist.cpu()
+    ctx = wk.ctx_lens.cpu()
+    W_ = wk.head_dim // 32
+    qs, ks, vs_rows, lens, scales, rows = [], [], [], [], [], []
+    vsc = wk.v_scale.cpu()
+    for it in items:
+        q_idx, bh = int(wl[it, 0]), int(wl[it, 1])
+        L = min(int(ctx[bh]), wk.num_blocks * wk.block_size)
+        if wk.causal:
+            L = min(L, q_idx + 1)
+        t = torch.arange(L, device=wk.k.device)
+        page = t // wk.block_size
+        if wk.block_tables.numel():
+            ids = wk.block_tables[bh].to(torch.int64)[page]
+        else:
+            ids = bh * wk.num_blocks + page
+        slots = ids * wk.block_size + t % wk.block_size
+        ks.append(wk.k[slots].cpu())
+        vs_rows.append(wk.v[slots].cpu())
+        qs.append(wk.q[bh * wk.seq_q + q_idx].cpu().view(1, W_))
+        lens.append(L)
+        scales.append(float(vsc[0] if vsc.numel() == 1 else vsc[bh % vsc.numel()]))
+        rows.append(bh * wk.seq_q + q_idx)
+    n = len(items)
+    Lmax = max(lens)
+    kk = torch.zeros(n * Lmax, W_, dtype=torch.int32)
+    vv = torch.zeros(n * Lmax, wk.head_dim, dtype=torch.uint8)
+    for i in range(n):
+        kk[i * Lmax: i * Lmax + lens[i]] = ks[i]
+        vv[i * Lmax: i * Lmax + lens[i]] = vs_rows[i]
+    sc = torch.tensor(scales, dtype=torch.float32)
+    if sc.numel() == kk.shape[0]:  # keep the per-(item) scale mode unambiguous
+        sc = torch.cat([sc, sc[:1]])
+    wl2 = W.dense_worklist(n, 1, "cpu")
+    wl2[:, 0] = 0
+    sub = W.Workload(name=wk.name + "_subset", worklist=wl2, q=torch.cat(qs), k=kk, v=vv, v_scale=sc,
+                     ctx_lens=torch.tensor(lens, dtype=torch.int32), block_tables=torch.zeros(0, dtype=torch.int32),
+                     seq_q=1, head_dim=wk.head_dim, block_size=Lmax, num_blocks=1, causal=False,
+                     o_dtype=torch.float32, batch=1, heads=n, inv_sqrt_d=wk.inv_sqrt_d)
+    return sub, rows
+
+
+def test_decode_config_full_size_sampled_rows(hyperion, oracle):
+    _sampled_check(hyperion, oracle, "decode")
+
+
+def test_paged_decode_config_full_size_sampled_rows(hyperion, oracle):
+    _sampled_check(hyperion, oracle, "paged_decode")
