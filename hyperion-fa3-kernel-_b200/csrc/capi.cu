@@ -41,6 +41,7 @@ struct DevInfo {
   int row_smem_128 = 0, row_smem_256 = 0;
   int tile_ctas = 0, tile_smem = 0;
   bool tile_ok = false;
+  std::string tile_why;  // why the tile kernel is unavailable ("" when it is)
 };
 
 constexpr int kMaxDevices = 64;
@@ -72,10 +73,12 @@ int get_dev(const DevInfo** out) {
     if (rc) return rc;
     rc = setup_row<256>(di.row_ctas_256, di.row_smem_256);
     if (rc) return rc;
-    rc = hyp::tile::setup(di.tile_ctas, di.tile_smem);
+    const char* why = "";
+    rc = hyp::tile::setup(di.tile_ctas, di.tile_smem, &why);
     di.tile_ok = (rc == HYPERION_OK);
     if (!di.tile_ok) {
       di.tile_ctas = 0;
+      di.tile_why = why;
       cudaGetLastError();
     }
     di.ready = true;
@@ -144,6 +147,7 @@ int hyperion_launch_info(int32_t* out, int32_t n) {
   const int32_t v[7] = {di->n_sm, di->row_ctas_128, di->row_smem_128, di->tile_ctas, di->tile_smem,
                         di->row_ctas_256, di->tile_ok ? 1 : 0};
   for (int i = 0; i < n && i < 7; ++i) out[i] = v[i];
+  if (!di->tile_ok) g_last_error = "tile kernel unavailable: " + di->tile_why;
   return HYPERION_OK;
 }
 
@@ -242,7 +246,8 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   if (path == HYPERION_PATH_AUTO) path = (tile_fits && seq_q >= 64) ? HYPERION_PATH_TILE : HYPERION_PATH_ROW;
   if (path == HYPERION_PATH_TILE && !tile_fits)
     return fail(HYPERION_ERR_UNSUPPORTED,
-                "tile path needs head_dim 128, a per-tensor or per-head V scale and a device that loaded it");
+                ("tile path needs head_dim 128, a per-tensor or per-head V scale and a device that loaded it" +
+                 (di->tile_ok ? std::string() : "; " + di->tile_why)).c_str());
 
   cudaError_t e = cudaMemsetAsync(ws + hyp::kWsCounters, 0, 64, st);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(counters)");

@@ -111,6 +111,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// mbar_wait for a whole warp: every lane waits, and the outcome is the same in all
+// 32 lanes (a timeout in one lane fails the wait for the warp), so a warp never
+// splits across a __syncwarp or a .sync.aligned instruction after a timeout.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                               uint32_t* err) {
+  const bool ok = mbar_wait(bar, parity, abort, err);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // Bounded wait that ignores the abort flag: used on the way out of an aborted CTA
 // to let copies already in flight land before the CTA's shared memory is released.
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {

@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kThreads, 5) row_fwd_kernel(FwdParams p, int t
       t = __shfl_sync(0xffffffffu, t, 0);
       const int unit = (t < total_units) ? t : -1;
       const int us = ucount & 1;
-      if (!mbar_wait(&sm.unit_empty[us], ((ucount >> 1) & 1) ^ 1, abort, p.err)) break;
+      if (!mbar_wait_warp(&sm.unit_empty[us], ((ucount >> 1) & 1) ^ 1, abort, p.err)) break;
       int item = 0, split = 0, k_lo = 0, k_hi = 0, bh = 0, q_idx = 0;
       bool valid = false;
       if (unit >= 0) {
@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 5) row_fwd_kernel(FwdParams p, int t
       bool aborted = false;
       for (int k0 = k_lo; k0 < k_hi; k0 += kKeysPerStage) {
         const int s = it % kStages;
-        if (!mbar_wait(&sm.empty[s], ((it / kStages) & 1) ^ 1, abort, p.err)) {
+        if (!mbar_wait_warp(&sm.empty[s], ((it / kStages) & 1) ^ 1, abort, p.err)) {
           aborted = true;
           break;
         }
@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 5) row_fwd_kernel(FwdParams p, int t
     uint32_t ucount = 0;
     for (;;) {
       const int us = ucount & 1;
-      if (!mbar_wait(&sm.unit_full[us], (ucount >> 1) & 1, abort, p.err)) break;
+      if (!mbar_wait_warp(&sm.unit_full[us], (ucount >> 1) & 1, abort, p.err)) break;
       const UnitSlot sl = sm.slot[us];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.unit_empty[us]);
@@ -256,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 5) row_fwd_kernel(FwdParams p, int t
       bool aborted = false;
       for (int k0 = sl.k_lo; k0 < sl.k_hi; k0 += kKeysPerStage) {
         const int s = it % kStages;
-        if (!mbar_wait(&sm.full[s], (it / kStages) & 1, abort, p.err)) {
+        if (!mbar_wait_warp(&sm.full[s], (it / kStages) & 1, abort, p.err)) {
           aborted = true;
           break;
         }

@@ -1,18 +1,729 @@
-// tile_kernel.cuh -- 128-row tcgen05 tile kernel (prefill path).
+// tile_kernel.cuh -- 128-row tcgen05 tile kernel: the prefill path.
+//
+// One CTA per SM, persistent.  A unit of work is a chunk of 256 consecutive work
+// items (two 128-row Q tiles) of one (batch, head) row `bh`; chunks are taken
+// with an atomic ticket in the caller's workspace (the reference's g_work_counter
+// work stealing, hyperion_fa3_production_final.py:236-243, :332-336), the last
+// chunks first so that, for causal prefill in (bh, q) order, the longest rows go
+// out first.  For every 128-key tile of the unit's KV range:
+//
+//   loader warp    cp.async.bulk of the raw page pieces (sign bits 16 B/key, FP8
+//                  codes 128 B/key) into a 3-stage ring, with the key-valid mask
+//                  (context length, page ids inside the pool; :402-411, :479-486);
+//   converters     (4 warps) sign bits -> e4m3 +-1 bytes in the 128B-swizzled
+//                  K-major layout; FP8 codes -> f16 (the reference's decode,
+//                  :122-141, divided by 256, exact) in the 128B-swizzled MN-major
+//                  layout; Q rows of the unit likewise, once per unit;
+//   MMA warp       S_t = Q_t K^T as a kind::f8f6f4 tcgen05.mma (the +-1 products
+//                  sum to D - 2*popcount(q XOR k) exactly in the f32 accumulator,
+//                  README.md:22), then O_t += P_t V as a kind::f16 MMA with P read
+//                  from TMEM; tcgen05.commit hands each result to its consumer;
+//   softmax WG t   (4 warps per Q tile, one thread per row = TMEM lane) reads S,
+//                  applies the masks (causal: key > q_idx, :483-486), keeps the
+//                  running max with the reference's online update (:544-572)
+//                  rescaling O in TMEM only when the max grows by more than
+//                  2^8, writes P as f16 back into TMEM over S, and at the end
+//                  of the unit finalises O = acc * (l > 1e-6 ? 1/l : 1) (:582-593).
+//
+// TMEM (512 columns): tile t uses S/P at [256t, 256t+128) and O at [256t+128, 256t+256).
+// Every mbarrier wait is bounded; on a timeout the CTA raises
+// HYPERION_DEVERR_WAIT_TIMEOUT, lets in-flight copies and MMAs land, frees TMEM
+// and exits.
 #pragma once
 
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace hyp {
 namespace tile {
 
-inline int setup(int& ctas, int& smem) {
-  ctas = 0;
-  smem = 0;
-  return HYPERION_ERR_UNSUPPORTED;
+constexpr int kRows = 128;
+constexpr int kQTiles = 2;
+constexpr int kChunk = kRows * kQTiles;
+constexpr int kKeys = 128;
+constexpr int kRawStages = 3;
+constexpr int kKvStages = 2;
+constexpr int kMmaWarp = 8;
+constexpr int kLoadWarp = 9;
+constexpr int kConvWarp0 = 10;
+constexpr int kConvWarps = 4;
+constexpr int kThreads = 32 * (kConvWarp0 + kConvWarps);  // 448
+constexpr int kSchedConsumers = 4 * kQTiles + 1 + kConvWarps;  // warps that read each unit
+constexpr uint32_t kTmemCols = 512;
+// Lazy rescale threshold: P = exp(s - m) may grow to 2^8 before the running max
+// is moved (8 / log2(e) in score units), well inside the f16 range of P.
+constexpr float kTauS = 5.545177444479562f;
+
+struct UnitInfo {
+  int kind;     // 0 stop, 1 work
+  int entry0;   // first work item of the chunk
+  int n_entries;
+  int seg_lo;   // rows [seg_lo, seg_hi) of the chunk belong to this unit
+  int seg_hi;
+  int bh;
+  int ctx;      // clamped context length of bh
+  int kv_len;   // keys [0, kv_len) are loaded
+  int n_tiles;
+  int pad[3];
+};
+
+struct Smem {
+  alignas(1024) uint8_t q[kQTiles][kRows * 128];
+  alignas(1024) uint8_t kt[kKvStages][kKeys * 128];
+  alignas(1024) uint8_t vt[kKvStages][kKeys * 256];
+  alignas(128) uint8_t raw_k[kRawStages][kKeys * 16];
+  alignas(128) uint8_t raw_v[kRawStages][kKeys * 128];
+  uint32_t raw_mask[kRawStages][4];
+  uint32_t kv_mask[kKvStages][4];
+  UnitInfo unit[2];
+  alignas(8) uint64_t sched_full[2];
+  alignas(8) uint64_t sched_empty[2];
+  alignas(8) uint64_t raw_full[kRawStages];
+  alignas(8) uint64_t raw_empty[kRawStages];
+  alignas(8) uint64_t kv_full[kKvStages];
+  alignas(8) uint64_t kv_empty[kKvStages];
+  alignas(8) uint64_t q_full;
+  alignas(8) uint64_t q_empty;
+  alignas(8) uint64_t s_full[kQTiles];
+  alignas(8) uint64_t p_full[kQTiles];
+  alignas(8) uint64_t o_full[kQTiles];
+  alignas(8) uint64_t o_empty[kQTiles];
+  alignas(8) uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + alignment slack of the dynamic base
+
+// 16 sign bits -> 16 e4m3 bytes: bit 1 -> +1.0 (0x38), bit 0 -> -1.0 (0xB8).  The
+// multiply spreads the 4 bits of a nibble to bit 7 of 4 bytes (no carries: the
+// partial products are 7 bits apart).
+__device__ __forceinline__ uint4 expand16(uint32_t b) {
+  uint4 o;
+  o.x = (((b & 0xFu) * 0x10204080u) & 0x80808080u) ^ 0xB8B8B8B8u;
+  o.y = ((((b >> 4) & 0xFu) * 0x10204080u) & 0x80808080u) ^ 0xB8B8B8B8u;
+  o.z = ((((b >> 8) & 0xFu) * 0x10204080u) & 0x80808080u) ^ 0xB8B8B8B8u;
+  o.w = ((((b >> 12) & 0xFu) * 0x10204080u) & 0x80808080u) ^ 0xB8B8B8B8u;
+  return o;
 }
 
-inline int launch(const FwdParams&, int, int, int, cudaStream_t, int*) { return HYPERION_ERR_UNSUPPORTED; }
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+// Four FP8 codes -> two f16x2 words in dim order, each value the reference's decode / 256.
+__device__ __forceinline__ void fp8x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t s = prmt(w, 0u, 0x3120u);  // bytes b0 b2 b1 b3
+  lo = fp8x2_even_to_f16x2_div256(s);       // {b0, b1}
+  hi = fp8x2_odd_to_f16x2_div256(s);        // {b2, b3}
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Byte offset of 16-byte chunk `c` of row `r` in a 128B-swizzled tile of 128-byte rows.
+__device__ __forceinline__ uint32_t sw128_off(uint32_t r, uint32_t c) {
+  return (r >> 3) * 1024u + (r & 7u) * 128u + ((c ^ (r & 7u)) << 4);
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %2, %1;" : "=r"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+__device__ __forceinline__ void store_row32(void* o, int dtype, long long base, const float (&v)[32]) {
+  if (dtype == HYPERION_DTYPE_F32) {
+    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(o) + base);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else if (dtype == HYPERION_DTYPE_BF16) {
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(o) + base);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * i + 2 * k], v[8 * i + 2 * k + 1]);
+        w[k] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(o) + base);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      dst[i] = make_uint4(pack_f16x2(v[8 * i], v[8 * i + 1]), pack_f16x2(v[8 * i + 2], v[8 * i + 3]),
+                          pack_f16x2(v[8 * i + 4], v[8 * i + 5]), pack_f16x2(v[8 * i + 6], v[8 * i + 7]));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_chunks = (p.total_work + kChunk - 1) / kChunk;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.sched_full[i], 1);
+      mbar_init(&sm.sched_empty[i], kSchedConsumers);
+    }
+    for (int i = 0; i < kRawStages; ++i) {
+      mbar_init(&sm.raw_full[i], 1);
+      mbar_init(&sm.raw_empty[i], kConvWarps);
+    }
+    for (int i = 0; i < kKvStages; ++i) {
+      mbar_init(&sm.kv_full[i], kConvWarps);
+      mbar_init(&sm.kv_empty[i], 1);
+    }
+    mbar_init(&sm.q_full, kConvWarps);
+    mbar_init(&sm.q_empty, 1);
+    for (int t = 0; t < kQTiles; ++t) {
+      mbar_init(&sm.s_full[t], 1);
+      mbar_init(&sm.p_full[t], 4);
+      mbar_init(&sm.o_full[t], 1);
+      mbar_init(&sm.o_empty[t], 4);
+    }
+    mbar_init(&sm.drain, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tc::tmem_alloc(&sm.tmem_base, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = sm.tmem_base;
+  volatile int* abort = &sm.abort;
+
+  if (warp == kLoadWarp) {
+    // ================================================================ loader
+    const uint64_t pol = policy_evict_last();
+    uint32_t uc = 0, rit = 0;
+    const long long cap = (long long)p.num_blocks * p.block_size;
+    // Ticket order: in a (bh, q_idx)-ordered worklist chunk c holds q rows
+    // [256*(c % cpb), ...) of its bh, and causal cost grows with that position.
+    // Tickets walk the positions from the last to the first, all bh at each
+    // position, so the most expensive chunks go first and the cheap ones fill
+    // the tail.  Any worklist order stays correct; only the balance depends on it.
+    const int cpb = max(1, (p.seq_q + kChunk - 1) / kChunk);
+    const int groups = (n_chunks + cpb - 1) / cpb;
+    const int n_tickets = groups * cpb;
+    bool stop = false;
+    while (!stop) {
+      int c = -1;
+      for (;;) {
+        int t = 0;
+        if (lane == 0) t = (int)atomicAdd(&p.counters[1], 1u);
+        t = __shfl_sync(0xffffffffu, t, 0);
+        if (t >= n_tickets) break;
+        const int qr = t / groups;
+        const int g = t - qr * groups;
+        const int cand = g * cpb + (cpb - 1 - qr);
+        if (cand < n_chunks) {
+          c = cand;
+          break;
+        }
+      }
+      if (c < 0) {
+        if (!mbar_wait_warp(&sm.sched_empty[uc & 1], ((uc >> 1) & 1) ^ 1, abort, p.err)) break;
+        if (lane == 0) {
+          sm.unit[uc & 1].kind = 0;
+          mbar_arrive(&sm.sched_full[uc & 1]);
+        }
+        ++uc;
+        break;
+      }
+      const int e0 = c * kChunk;
+      const int ne = min(kChunk, p.total_work - e0);
+      int seg_lo = 0;
+      while (seg_lo < ne) {
+        const int bh0 = __ldg(&p.worklist[e0 + seg_lo].y);
+        int seg_hi = ne;
+        for (int base = seg_lo + 1; base < ne; base += 32) {
+          const int r = base + lane;
+          const bool diff = (r < ne) && (__ldg(&p.worklist[e0 + r].y) != bh0);
+          const unsigned b = __ballot_sync(0xffffffffu, diff);
+          if (b) {
+            seg_hi = base + __ffs(b) - 1;
+            break;
+          }
+        }
+        const bool bh_ok = bh0 >= 0 && bh0 < p.n_bh;
+        int maxq = -1;
+        for (int r = seg_lo + lane; r < seg_hi; r += 32) {
+          const int qi = __ldg(&p.worklist[e0 + r].x);
+          if (bh_ok && qi >= 0 && qi < p.seq_q) {
+            maxq = max(maxq, qi);
+          } else {
+            raise_error(p.err, HYPERION_DEVERR_BAD_ITEM);
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) maxq = max(maxq, __shfl_xor_sync(0xffffffffu, maxq, o));
+        if (!bh_ok || maxq < 0) {
+          seg_lo = seg_hi;
+          continue;
+        }
+        int ctx = __ldg(p.ctx_lens + bh0);
+        if (ctx < 0) {
+          if (lane == 0) raise_error(p.err, HYPERION_DEVERR_NEG_CTX);
+          ctx = 0;
+        }
+        if ((long long)ctx > cap) {
+          if (lane == 0) raise_error(p.err, HYPERION_DEVERR_CTX_OVERFLOW);
+          ctx = (int)cap;
+        }
+        const int kv_len = p.causal ? min(ctx, maxq + 1) : ctx;
+        const int n_tiles = (kv_len + kKeys - 1) / kKeys;
+        if (!mbar_wait_warp(&sm.sched_empty[uc & 1], ((uc >> 1) & 1) ^ 1, abort, p.err)) {
+          stop = true;
+          break;
+        }
+        if (lane == 0) {
+          UnitInfo& u = sm.unit[uc & 1];
+          u.kind = 1;
+          u.entry0 = e0;
+          u.n_entries = ne;
+          u.seg_lo = seg_lo;
+          u.seg_hi = seg_hi;
+          u.bh = bh0;
+          u.ctx = ctx;
+          u.kv_len = kv_len;
+          u.n_tiles = n_tiles;
+          mbar_arrive(&sm.sched_full[uc & 1]);
+        }
+        ++uc;
+        for (int j = 0; j < n_tiles; ++j) {
+          const int r = rit % kRawStages;
+          if (!mbar_wait_warp(&sm.raw_empty[r], ((rit / kRawStages) & 1) ^ 1, abort, p.err)) {
+            stop = true;
+            break;
+          }
+          const int k0 = j * kKeys;
+          const int n = min(kKeys, kv_len - k0);
+          const int bs = p.block_size;
+          const int p0 = k0 / bs;
+          const int np = (k0 + n - 1) / bs - p0 + 1;
+          uint32_t bytes = 0;
+          uint32_t mk[4] = {0u, 0u, 0u, 0u};
+          for (int i = lane; i < np; i += 32) {
+            const int page = p0 + i;
+            const int lo = max(k0, page * bs) - k0;
+            const int hi = min(k0 + n, (page + 1) * bs) - k0;
+            if (page_block_id(p, bh0, page) >= 0) {
+              bytes += (uint32_t)(hi - lo) * (16u + 128u);
+#pragma unroll
+              for (int w = 0; w < 4; ++w) {
+                const int a = max(lo, 32 * w), b = min(hi, 32 * w + 32);
+                if (a < b) mk[w] |= ((b - a == 32) ? 0xFFFFFFFFu : ((1u << (b - a)) - 1u)) << (a - 32 * w);
+              }
+            } else {
+              raise_error(p.err, HYPERION_DEVERR_BAD_BLOCK);
+            }
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
+#pragma unroll
+            for (int w = 0; w < 4; ++w) mk[w] |= __shfl_xor_sync(0xffffffffu, mk[w], o);
+          }
+          if (lane == 0) {
+#pragma unroll
+            for (int w = 0; w < 4; ++w) sm.raw_mask[r][w] = mk[w];
+            if (bytes) {
+              mbar_arrive_expect_tx(&sm.raw_full[r], bytes);
+            } else {
+              mbar_arrive(&sm.raw_full[r]);
+            }
+          }
+          __syncwarp();
+          for (int i = lane; i < np; i += 32) {
+            const int page = p0 + i;
+            const int lo = max(k0, page * bs);
+            const int hi = min(k0 + n, (page + 1) * bs);
+            const long long id = page_block_id(p, bh0, page);
+            if (id >= 0) {
+              const long long slot0 = id * bs + (lo - page * bs);
+              const uint32_t cnt = (uint32_t)(hi - lo);
+              bulk_g2s_stream(&sm.raw_k[r][(lo - k0) * 16], p.k + slot0 * 4, cnt * 16u, &sm.raw_full[r], pol);
+              bulk_g2s_stream(&sm.raw_v[r][(lo - k0) * 128], p.v + slot0 * 128, cnt * 128u, &sm.raw_full[r], pol);
+            }
+          }
+          ++rit;
+        }
+        if (stop) break;
+        seg_lo = seg_hi;
+      }
+    }
+    if (*abort && lane == 0) {
+      for (uint32_t i = (rit > (uint32_t)kRawStages ? rit - kRawStages : 0u); i < rit; ++i)
+        mbar_drain(&sm.raw_full[i % kRawStages], (i / kRawStages) & 1);
+    }
+  } else if (warp >= kConvWarp0) {
+    // ================================================================ converters
+    const int ct = threadIdx.x - 32 * kConvWarp0;  // 0..127
+    uint32_t uc = 0, rit = 0, kvit = 0, uq = 0;
+    const uint32_t q_base = smem_u32(&sm.q[0][0]);
+    for (;;) {
+      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) break;
+      const UnitInfo u = sm.unit[uc & 1];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.sched_empty[uc & 1]);
+      ++uc;
+      if (u.kind == 0) break;
+      if (u.n_tiles == 0) continue;
+      // ---- Q rows of the unit -> e4m3 +-1, K-major SW128
+      if (!mbar_wait_warp(&sm.q_empty, (uq & 1) ^ 1, abort, p.err)) break;
+#pragma unroll
+      for (int i = 0; i < kQTiles; ++i) {
+        const int r = i * kRows + ct;
+        uint4 bits = make_uint4(0u, 0u, 0u, 0u);
+        if (r >= u.seg_lo && r < u.seg_hi) {
+          const int qi = __ldg(&p.worklist[u.entry0 + r].x);
+          if (qi >= 0 && qi < p.seq_q)
+            bits = __ldg(reinterpret_cast<const uint4*>(p.q + ((long long)u.bh * p.seq_q + qi) * 4));
+        }
+        const uint32_t words[4] = {bits.x, bits.y, bits.z, bits.w};
+        const uint32_t tb = q_base + i * (kRows * 128);
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          st_shared_v4(tb + sw128_off(ct, c), expand16((words[c >> 1] >> (16 * (c & 1))) & 0xFFFFu));
+      }
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.q_full);
+      ++uq;
+      // ---- KV tiles
+      bool ab = false;
+      for (int j = 0; j < u.n_tiles; ++j) {
+        const int r = rit % kRawStages;
+        const int s = kvit % kKvStages;
+        if (!mbar_wait_warp(&sm.raw_full[r], (rit / kRawStages) & 1, abort, p.err) ||
+            !mbar_wait_warp(&sm.kv_empty[s], ((kvit / kKvStages) & 1) ^ 1, abort, p.err)) {
+          ab = true;
+          break;
+        }
+        // K: thread ct owns key ct.
+        {
+          const uint4 kb = *reinterpret_cast<const uint4*>(&sm.raw_k[r][ct * 16]);
+          const uint32_t words[4] = {kb.x, kb.y, kb.z, kb.w};
+          const uint32_t tb = smem_u32(&sm.kt[s][0]);
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            st_shared_v4(tb + sw128_off(ct, c), expand16((words[c >> 1] >> (16 * (c & 1))) & 0xFFFFu));
+        }
+        // V: 2048 (key, 8-dim chunk) tasks, 16 per thread; 16 lanes cover one key row.
+        {
+          const uint32_t vb = smem_u32(&sm.vt[s][0]);
+#pragma unroll 4
+          for (int i = 0; i < 16; ++i) {
+            const int task = ct + 128 * i;
+            const int key = task >> 4;
+            const int c8 = task & 15;
+            const uint2 w = *reinterpret_cast<const uint2*>(&sm.raw_v[r][key * 128 + c8 * 8]);
+            uint4 o;
+            fp8x4_to_f16x4(w.x, o.x, o.y);
+            fp8x4_to_f16x4(w.y, o.z, o.w);
+            st_shared_v4(vb + (c8 >> 3) * 16384u + sw128_off(key, c8 & 7), o);
+          }
+        }
+        if (ct < 4) sm.kv_mask[s][ct] = sm.raw_mask[r][ct];
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&sm.kv_full[s]);
+          mbar_arrive(&sm.raw_empty[r]);
+        }
+        ++rit;
+        ++kvit;
+      }
+      if (ab) break;
+    }
+  } else if (warp == kMmaWarp) {
+    // ================================================================ MMA issuer
+    if (lane == 0) {
+      uint32_t uc = 0, kvit = 0, uq = 0, uo = 0;
+      uint32_t pc[kQTiles] = {0u, 0u};
+      const uint32_t q_base = smem_u32(&sm.q[0][0]);
+      const uint32_t k_base = smem_u32(&sm.kt[0][0]);
+      const uint32_t v_base = smem_u32(&sm.vt[0][0]);
+      bool ab = false;
+      auto qk = [&](int t, int s) {
+        const uint32_t d = tmem + (uint32_t)(t * 256);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t ad = tc::sw128_desc(q_base + t * (kRows * 128) + kk * 32, 16, 1024);
+          const uint64_t bd = tc::sw128_desc(k_base + s * (kKeys * 128) + kk * 32, 16, 1024);
+          tc::mma_f8f6f4_ss(d, ad, bd, tc::kIdescQK, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto pv = [&](int t, int s, bool acc) {
+        const uint32_t d = tmem + (uint32_t)(t * 256 + 128);
+        const uint32_t a = tmem + (uint32_t)(t * 256);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t bd = tc::sw128_desc(v_base + s * (kKeys * 256) + kk * 2048, 16384, 1024);
+          tc::mma_f16_ts(d, a + kk * 8, bd, tc::kIdescPV, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      for (;;) {
+        if (!mbar_wait(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) break;
+        const UnitInfo u = sm.unit[uc & 1];
+        mbar_arrive(&sm.sched_empty[uc & 1]);
+        ++uc;
+        if (u.kind == 0) break;
+        const int n = u.n_tiles;
+        if (n == 0) continue;
+        if (!mbar_wait(&sm.q_full, uq & 1, abort, p.err)) break;
+        ++uq;
+        int s = kvit % kKvStages;
+        if (!mbar_wait(&sm.kv_full[s], (kvit / kKvStages) & 1, abort, p.err)) break;
+        tc::fence_after_sync();
+        for (int t = 0; t < kQTiles; ++t) {
+          qk(t, s);
+          tc::commit(&sm.s_full[t]);
+        }
+        if (n == 1) tc::commit(&sm.q_empty);
+        for (int j = 0; j < n && !ab; ++j) {
+          s = (kvit + j) % kKvStages;
+          const uint32_t nxt = kvit + j + 1;
+          for (int t = 0; t < kQTiles; ++t) {
+            if (!mbar_wait(&sm.p_full[t], pc[t] & 1, abort, p.err)) {
+              ab = true;
+              break;
+            }
+            ++pc[t];
+            if (j == 0 && !mbar_wait(&sm.o_empty[t], (uo & 1) ^ 1, abort, p.err)) {
+              ab = true;
+              break;
+            }
+            tc::fence_after_sync();
+            pv(t, s, j > 0);
+            if (j == n - 1) tc::commit(&sm.o_full[t]);
+            if (t == kQTiles - 1) tc::commit(&sm.kv_empty[s]);
+            if (j + 1 < n) {
+              const int s2 = nxt % kKvStages;
+              if (t == 0) {
+                if (!mbar_wait(&sm.kv_full[s2], (nxt / kKvStages) & 1, abort, p.err)) {
+                  ab = true;
+                  break;
+                }
+                tc::fence_after_sync();
+              }
+              qk(t, s2);
+              tc::commit(&sm.s_full[t]);
+              if (t == kQTiles - 1 && j + 2 == n) tc::commit(&sm.q_empty);
+            }
+          }
+        }
+        if (ab) break;
+        kvit += n;
+        ++uo;
+      }
+      // Every MMA issued must land before TMEM is released.
+      tc::commit(&sm.drain);
+      mbar_drain(&sm.drain, 0);
+    }
+    __syncwarp();
+  } else {
+    // ================================================================ softmax (warps 0-7)
+    const int t = warp >> 2;         // Q tile
+    const int wq = warp & 3;         // TMEM lane quarter
+    const int row = wq * 32 + lane;  // row of the tile = TMEM lane
+    const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+    const uint32_t s_col = tmem + lane_off + (uint32_t)(t * 256);
+    const uint32_t o_col = s_col + 128;
+    const float c_scale = p.inv_sqrt_d;
+    const float k2 = c_scale * kLog2e;
+    uint32_t uc = 0, kvit = 0, sc = 0, oc = 0;
+    for (;;) {
+      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) break;
+      const UnitInfo u = sm.unit[uc & 1];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.sched_empty[uc & 1]);
+      ++uc;
+      if (u.kind == 0) break;
+      const int r = t * kRows + row;
+      int q_idx = -1;
+      if (r >= u.seg_lo && r < u.seg_hi) {
+        const int qi = __ldg(&p.worklist[u.entry0 + r].x);
+        if (qi >= 0 && qi < p.seq_q) q_idx = qi;
+      }
+      const bool row_ok = q_idx >= 0;
+      const long long o_base = row_ok ? ((long long)u.bh * p.seq_q + q_idx) * 128 : 0;
+      const int item = u.entry0 + r;
+      if (u.n_tiles == 0) {
+        if (row_ok) {
+          float z[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) z[i] = 0.f;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) store_row32(p.o, p.o_dtype, o_base + 32 * c, z);
+        }
+        continue;
+      }
+      const int row_end = row_ok ? (p.causal ? min(u.ctx, q_idx + 1) : u.ctx) : 0;
+      float m = -INFINITY, l = 0.f;
+      bool ab = false;
+      for (int j = 0; j < u.n_tiles; ++j) {
+        const int s = kvit % kKvStages;
+        if (!mbar_wait_warp(&sm.s_full[t], sc & 1, abort, p.err) ||
+            !mbar_wait_warp(&sm.kv_full[s], (kvit / kKvStages) & 1, abort, p.err)) {
+          ab = true;
+          break;
+        }
+        ++sc;
+        tc::fence_after_sync();
+        const int k0 = j * kKeys;
+        uint32_t mk[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) mk[w] = sm.kv_mask[s][w];
+        const bool full = (mk[0] & mk[1] & mk[2] & mk[3]) == 0xFFFFFFFFu && k0 + kKeys <= row_end;
+        // ---- pass 1: tile max of the raw integer scores
+        float mx = -INFINITY, mn = INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tc::ld32(s_col + 32 * c, v);
+          tc::ld_wait();
+          const uint32_t bits = full ? 0xFFFFFFFFu : mk[c];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float x = __uint_as_float(v[i]);
+            const bool ok = full || (((bits >> i) & 1u) && (k0 + 32 * c + i < row_end));
+            mx = ok ? fmaxf(mx, x) : mx;
+            mn = ok ? fminf(mn, x) : mn;
+            if (p.debug_scores && ok) p.debug_scores[(long long)item * p.debug_ld + k0 + 32 * c + i] = (int)x;
+          }
+        }
+        // tile max in score units (s = integer score * inv_sqrt_d)
+        const float mt = (mx == -INFINITY) ? -INFINITY : (c_scale >= 0.f ? mx * c_scale : mn * c_scale);
+        const bool need = mt > m + kTauS;
+        const bool resc = need && (m != -INFINITY);
+        const float alpha = resc ? ex2_approx((m - mt) * kLog2e) : 1.f;
+        if (need) m = mt;
+        l *= alpha;
+        if (__any_sync(0xffffffffu, resc)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t v[32];
+            tc::ld32(o_col + 32 * c, v);
+            tc::ld_wait();
+            uint32_t a0[16], a1[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              a0[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+              a1[i] = __float_as_uint(__uint_as_float(v[16 + i]) * alpha);
+            }
+            tc::st16(o_col + 32 * c, a0);
+            tc::st16(o_col + 32 * c + 16, a1);
+          }
+          tc::st_wait();
+        }
+        // ---- pass 2: P = exp(s - m) as f16 over S's columns, l += P
+        const float bias = (m == -INFINITY) ? 0.f : -m * kLog2e;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tc::ld32(s_col + 32 * c, v);
+          tc::ld_wait();
+          const uint32_t bits = full ? 0xFFFFFFFFu : mk[c];
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float pr[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int ii = 2 * i + h;
+              const bool ok = full || (((bits >> ii) & 1u) && (k0 + 32 * c + ii < row_end));
+              const float e = ex2_approx(fmaf(__uint_as_float(v[ii]), k2, bias));
+              pr[h] = ok ? e : 0.f;
+              l += pr[h];
+            }
+            pk[i] = pack_f16x2(pr[0], pr[1]);
+          }
+          tc::st16(s_col + 16 * c, pk);
+        }
+        tc::st_wait();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_full[t]);
+        ++kvit;
+      }
+      if (ab) break;
+      // ---- epilogue: O row = acc * 256 * vscale / l
+      if (!mbar_wait_warp(&sm.o_full[t], oc & 1, abort, p.err)) break;
+      ++oc;
+      tc::fence_after_sync();
+      const float vs = (p.v_scale_mode == 0) ? __ldg(p.v_scale) : __ldg(p.v_scale + (u.bh % p.v_scale_numel));
+      const float scale = 256.f * vs * ((l > 1e-6f) ? 1.f / l : 1.f);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tc::ld32(o_col + 32 * c, v);
+        tc::ld_wait();
+        if (row_ok) {
+          float f[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]) * scale;
+          store_row32(p.o, p.o_dtype, o_base + 32 * c, f);
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.o_empty[t]);
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Sets the kernel's shared-memory limit and checks that one CTA fits on an SM.
+// On failure `why` names the step.
+inline int setup(int& ctas, int& smem, const char** why) {
+  smem = (int)kSmemBytes;
+  cudaError_t e = cudaFuncSetAttribute(tile_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) {
+    *why = cudaGetErrorString(e);
+    return HYPERION_ERR_CUDA;
+  }
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, tile_fwd_kernel, kThreads, smem);
+  if (e != cudaSuccess) {
+    *why = cudaGetErrorString(e);
+    return HYPERION_ERR_CUDA;
+  }
+  if (ctas < 1) {
+    *why = "occupancy calculator: no CTA of the tile kernel fits on an SM";
+    return HYPERION_ERR_UNSUPPORTED;
+  }
+  ctas = 1;  // one CTA per SM: the kernel allocates all 512 TMEM columns
+  return HYPERION_OK;
+}
+
+inline int launch(const FwdParams& p, int n_sm, int ctas, int smem, cudaStream_t st, int* grid_out) {
+  const int n_chunks = (p.total_work + kChunk - 1) / kChunk;
+  const int grid = std::min(n_chunks, n_sm * std::max(ctas, 1));
+  if (grid <= 0) return HYPERION_OK;
+  tile_fwd_kernel<<<grid, kThreads, smem, st>>>(p);
+  if (grid_out) *grid_out = grid;
+  return HYPERION_OK;
+}
 
 }  // namespace tile
 }  // namespace hyp

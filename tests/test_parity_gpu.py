@@ -234,3 +234,123 @@ def test_decode_config_full_size_sampled_rows(hyperion, oracle):
 
 def test_paged_decode_config_full_size_sampled_rows(hyperion, oracle):
     _sampled_check(hyperion, oracle, "paged_decode")
+
+
+# ----------------------------------------------------------------------------- tile path (tcgen05)
+def paged_copy(wk, page=16, seed=0):
+    """The same keys as a contiguous workload, moved into a shuffled pool of pages."""
+    n_bh = wk.n_bh
+    S = wk.block_size
+    pages = (S + page - 1) // page
+    g = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(n_bh * pages, generator=g)
+    k = torch.zeros(n_bh * pages * page, wk.k.shape[1], dtype=wk.k.dtype)
+    v = torch.zeros(n_bh * pages * page, wk.head_dim, dtype=wk.v.dtype)
+    bt = torch.zeros(n_bh, pages, dtype=torch.int32)
+    for bh in range(n_bh):
+        for pg in range(pages):
+            blk = int(perm[bh * pages + pg])
+            lo, hi = pg * page, min(S, (pg + 1) * page)
+            k[blk * page: blk * page + hi - lo] = wk.k[bh * S + lo: bh * S + hi]
+            v[blk * page: blk * page + hi - lo] = wk.v[bh * S + lo: bh * S + hi]
+            bt[bh, pg] = blk
+    return W.Workload(**{**wk.__dict__, "k": k, "v": v, "block_tables": bt, "block_size": page,
+                         "num_blocks": pages})
+
+
+def test_tile_path_is_available(hyperion):
+    assert hyperion.launch_info()["tile_available"] == 1
+
+
+@pytest.mark.parametrize("o_dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_tile_path_cpu_ref_config(hyperion, oracle, o_dtype):
+    wk = W.make_config("cpu_ref", device="cpu", exact=True)
+    o, err, _ = run(hyperion, wk, path="tile", o_dtype=o_dtype)
+    assert err == 0 and hyperion.last_call_info()["path"] == "tile"
+    check(oracle, wk, o)
+
+
+@pytest.mark.parametrize("scale_mode", ["tensor", "head", "bh"])
+def test_tile_path_causal_ragged_multisegment(hyperion, oracle, scale_mode):
+    # 300 rows per bh: chunks of 256 work items straddle (batch, head) rows.
+    wk = W.make_dense("c", 2, 3, 300, 300, causal=True, scale_mode=scale_mode, o_dtype=torch.float32, seed=21)
+    o, err, _ = run(hyperion, wk, path="tile")
+    assert err == 0
+    check(oracle, wk, o)
+
+
+def test_tile_path_noncausal_kv_longer_than_q(hyperion, oracle):
+    wk = W.make_dense("n", 1, 4, 130, 1000, causal=False, o_dtype=torch.float32, seed=22)
+    o, err, _ = run(hyperion, wk, path="tile")
+    assert err == 0
+    check(oracle, wk, o)
+
+
+def test_tile_path_scores_bit_exact(hyperion, oracle):
+    wk = W.make_dense("s", 1, 2, 256, 384, causal=True, o_dtype=torch.float32, seed=23)
+    L = 384
+    _, _, _, sc_ref = oracle.forward_workload_c(wk, scores_ld=L)
+    _, err, sc = run(hyperion, wk, path="tile", debug_ld=L)
+    assert err == 0
+    assert np.array_equal(sc, sc_ref)
+
+
+def test_tile_path_paged_prefill(hyperion, oracle):
+    dense = W.make_dense("pp", 2, 2, 200, 200, causal=True, o_dtype=torch.float32, seed=24)
+    wk = paged_copy(dense, page=16, seed=3)
+    o, err, _ = run(hyperion, wk, path="tile")
+    assert err == 0
+    check(oracle, wk, o)
+    check(oracle, dense, o)
+
+
+def test_tile_path_large_scores_force_rescale(hyperion, oracle):
+    # inv_sqrt_d = 1: scores span +-128, the running max moves by more than 2^8
+    # many times and O is rescaled in TMEM.
+    wk = W.make_dense("r", 1, 2, 256, 1024, causal=False, o_dtype=torch.float32, seed=25)
+    wk.inv_sqrt_d = 1.0
+    o, err, _ = run(hyperion, wk, path="tile")
+    assert err == 0
+    check(oracle, wk, o)
+
+
+def test_tile_path_short_and_empty_contexts(hyperion, oracle):
+    wk = W.make_dense("e", 1, 4, 256, 256, causal=False, o_dtype=torch.float32, seed=26)
+    wk.ctx_lens[0] = 0
+    wk.ctx_lens[1] = 1
+    wk.ctx_lens[2] = 129
+    o, err, _ = run(hyperion, wk, path="tile")
+    assert err == 0
+    assert np.all(o[0:256] == 0)
+    check(oracle, wk, o)
+
+
+def test_tile_path_bad_block_flag(hyperion, oracle):
+    dense = W.make_dense("b", 1, 2, 128, 128, causal=True, o_dtype=torch.float32, seed=27)
+    wk = paged_copy(dense, page=16, seed=4)
+    wk.block_tables[0, 3] = 1 << 29
+    o, err, _ = run(hyperion, wk, path="tile")
+    assert err & hyperion.DEVERR_BAD_BLOCK
+    check(oracle, wk, o)
+
+
+def test_tile_and_row_paths_agree(hyperion, oracle):
+    wk = W.make_dense("a", 2, 2, 384, 384, causal=True, o_dtype=torch.float32, seed=28)
+    o_t, e1, _ = run(hyperion, wk, path="tile")
+    o_r, e2, _ = run(hyperion, wk, path="row")
+    assert e1 == 0 and e2 == 0
+    ok, mx, mn = oracle.tolerance_check(o_t, o_r, MAX_ABS, MEAN_ABS)
+    assert ok, (mx, mn)
+
+
+def test_auto_path_picks_tile_for_prefill_and_row_for_decode(hyperion):
+    wk = W.make_dense("x", 1, 2, 128, 128, causal=True, o_dtype=torch.float32, seed=29)
+    run(hyperion, wk)
+    assert hyperion.last_call_info()["path"] == "tile"
+    wk2 = W.make_dense("y", 1, 2, 1, 128, o_dtype=torch.float32, seed=29)
+    run(hyperion, wk2)
+    assert hyperion.last_call_info()["path"] == "row"
+
+
+def test_prefill_config_full_size_sampled_rows(hyperion, oracle):
+    _sampled_check(hyperion, oracle, "prefill", n_rows=32, path="tile")
