@@ -136,15 +136,17 @@ __device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
   return r;
 }
 
-__device__ __forceinline__ void store_row32(void* o, int dtype, long long base, const float (&v)[32]) {
-  if (dtype == HYPERION_DTYPE_F32) {
+// Stores 16 consecutive output values of one row (f32, bf16 or f16).
+template <int kDtype>
+__device__ __forceinline__ void store_row16(void* o, long long base, const float (&v)[16]) {
+  if constexpr (kDtype == HYPERION_DTYPE_F32) {
     float4* dst = reinterpret_cast<float4*>(static_cast<float*>(o) + base);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-  } else if (dtype == HYPERION_DTYPE_BF16) {
+    for (int i = 0; i < 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else if constexpr (kDtype == HYPERION_DTYPE_BF16) {
     uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(o) + base);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 2; ++i) {
       uint32_t w[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -156,13 +158,161 @@ __device__ __forceinline__ void store_row32(void* o, int dtype, long long base, 
   } else {
     uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(o) + base);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 2; ++i) {
       dst[i] = make_uint4(pack_f16x2(v[8 * i], v[8 * i + 1]), pack_f16x2(v[8 * i + 2], v[8 * i + 3]),
                           pack_f16x2(v[8 * i + 4], v[8 * i + 5]), pack_f16x2(v[8 * i + 6], v[8 * i + 7]));
     }
   }
 }
 
+// Epilogue of one row: O = acc * scale from TMEM to global memory, 16 columns at a time.
+template <int kDtype>
+__device__ __forceinline__ void store_o_row(void* o, long long o_base, uint32_t o_col, float scale, bool row_ok) {
+#pragma unroll 1
+  for (int c = 0; c < 8; ++c) {
+    uint32_t v[16];
+    tc::ld16(o_col + 16 * c, v);
+    tc::ld_wait();
+    if (row_ok) {
+      float f[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) f[i] = __uint_as_float(v[i]) * scale;
+      store_row16<kDtype>(o, o_base + 16 * c, f);
+    }
+  }
+}
+
+__device__ __forceinline__ void store_zero_row(void* o, int dtype, long long o_base) {
+  float z[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) z[i] = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < 8; ++c) {
+    if (dtype == HYPERION_DTYPE_F32) {
+      store_row16<HYPERION_DTYPE_F32>(o, o_base + 16 * c, z);
+    } else if (dtype == HYPERION_DTYPE_BF16) {
+      store_row16<HYPERION_DTYPE_BF16>(o, o_base + 16 * c, z);
+    } else {
+      store_row16<HYPERION_DTYPE_F16>(o, o_base + 16 * c, z);
+    }
+  }
+}
+
+// Mask bits of chunk c (keys kbase + 32c .. +31) for a row whose keys end at row_end.
+__device__ __forceinline__ uint32_t chunk_bits(const uint32_t (&mk)[4], int c, int kbase, int row_end) {
+  const int lim = row_end - kbase - 32 * c;
+  const uint32_t lm = lim >= 32 ? 0xFFFFFFFFu : (lim <= 0 ? 0u : ((1u << lim) - 1u));
+  return mk[c] & lm;
+}
+
+// Max of this thread's row over the 128 S columns of the tile (raw integer scores).
+template <bool kMasked>
+__device__ __forceinline__ float row_tile_max(uint32_t s_col, const uint32_t (&mk)[4], int kbase, int row_end) {
+  float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
+#pragma unroll 2
+  for (int h = 0; h < 8; ++h) {
+    uint32_t v[16];
+    tc::ld16(s_col + 16 * h, v);
+    tc::ld_wait();
+    const uint32_t bits = kMasked ? (chunk_bits(mk, h >> 1, kbase, row_end) >> (16 * (h & 1))) : 0xFFFFu;
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+      float x0 = __uint_as_float(v[i]), x1 = __uint_as_float(v[i + 1]);
+      float x2 = __uint_as_float(v[i + 2]), x3 = __uint_as_float(v[i + 3]);
+      if (kMasked) {
+        x0 = ((bits >> i) & 1u) ? x0 : -INFINITY;
+        x1 = ((bits >> (i + 1)) & 1u) ? x1 : -INFINITY;
+        x2 = ((bits >> (i + 2)) & 1u) ? x2 : -INFINITY;
+        x3 = ((bits >> (i + 3)) & 1u) ? x3 : -INFINITY;
+      }
+      a0 = fmaxf(a0, x0);
+      a1 = fmaxf(a1, x1);
+      a2 = fmaxf(a2, x2);
+      a3 = fmaxf(a3, x3);
+    }
+  }
+  return fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
+}
+
+// P = 2^(S*k2 + bias) for this thread's row, packed to f16 pairs and stored over
+// the first 64 columns of S (the P of columns [16h, 16h+16) lands on columns
+// [8h, 8h+8), already read); returns the sum of P.
+template <bool kMasked>
+__device__ __forceinline__ float row_tile_p(uint32_t s_col, const uint32_t (&mk)[4], int kbase, int row_end,
+                                            float k2, float bias) {
+  float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+#pragma unroll 2
+  for (int h = 0; h < 8; ++h) {
+    uint32_t v[16];
+    tc::ld16(s_col + 16 * h, v);
+    tc::ld_wait();
+    const uint32_t bits = kMasked ? (chunk_bits(mk, h >> 1, kbase, row_end) >> (16 * (h & 1))) : 0xFFFFu;
+    uint32_t pk[8];
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+      float e0 = ex2_approx(fmaf(__uint_as_float(v[2 * i]), k2, bias));
+      float e1 = ex2_approx(fmaf(__uint_as_float(v[2 * i + 1]), k2, bias));
+      float e2 = ex2_approx(fmaf(__uint_as_float(v[2 * i + 2]), k2, bias));
+      float e3 = ex2_approx(fmaf(__uint_as_float(v[2 * i + 3]), k2, bias));
+      if (kMasked) {
+        e0 = ((bits >> (2 * i)) & 1u) ? e0 : 0.f;
+        e1 = ((bits >> (2 * i + 1)) & 1u) ? e1 : 0.f;
+        e2 = ((bits >> (2 * i + 2)) & 1u) ? e2 : 0.f;
+        e3 = ((bits >> (2 * i + 3)) & 1u) ? e3 : 0.f;
+      }
+      l0 += e0;
+      l1 += e1;
+      l2 += e2;
+      l3 += e3;
+      pk[i] = pack_f16x2(e0, e1);
+      pk[i + 1] = pack_f16x2(e2, e3);
+    }
+    tc::st8(s_col + 8 * h, pk);
+  }
+  return (l0 + l1) + (l2 + l3);
+}
+
+// O row *= alpha (lanes that need no rescale pass alpha = 1).
+__device__ __forceinline__ void rescale_row(uint32_t o_col, float alpha) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint32_t v[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(o_col + 16 * c)
+        : "memory");
+    tc::ld_wait();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+    tc::st16(o_col + 16 * c, v);
+  }
+  tc::st_wait();
+}
+
+// Debug export: the integer score of every key this row attends in the tile.
+__device__ __noinline__ void debug_row_scores(const FwdParams& p, uint32_t s_col, const uint32_t (&mk)[4], int kbase,
+                                              int row_end, int item) {
+  const bool flip = p.inv_sqrt_d < 0.f;
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t v[32];
+    tc::ld32(s_col + 32 * c, v);
+    tc::ld_wait();
+    const uint32_t bits = chunk_bits(mk, c, kbase, row_end);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if ((bits >> i) & 1u) {
+        const int x = (int)__uint_as_float(v[i]);
+        p.debug_scores[(long long)item * p.debug_ld + kbase + 32 * c + i] = flip ? -x : x;
+      }
+    }
+  }
+}
+
+template <bool kDebug>
 __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -394,6 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           if (qi >= 0 && qi < p.seq_q)
             bits = __ldg(reinterpret_cast<const uint4*>(p.q + ((long long)u.bh * p.seq_q + qi) * 4));
         }
+        if (p.inv_sqrt_d < 0.f) bits = make_uint4(~bits.x, ~bits.y, ~bits.z, ~bits.w);
         const uint32_t words[4] = {bits.x, bits.y, bits.z, bits.w};
         const uint32_t tb = q_base + i * (kRows * 128);
 #pragma unroll
@@ -544,39 +695,46 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
     const uint32_t s_col = tmem + lane_off + (uint32_t)(t * 256);
     const uint32_t o_col = s_col + 128;
-    const float c_scale = p.inv_sqrt_d;
-    const float k2 = c_scale * kLog2e;
+    // A negative inv_sqrt_d is folded into Q (the converters flip its bits), so the
+    // tile scores here are always multiplied by |inv_sqrt_d| and their max is a max.
+    const float cabs = fabsf(p.inv_sqrt_d);
+    const float k2 = cabs * kLog2e;
     uint32_t uc = 0, kvit = 0, sc = 0, oc = 0;
     for (;;) {
       if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) break;
-      const UnitInfo u = sm.unit[uc & 1];
+      int n_tiles, bh, row_end, item;
+      long long o_base;
+      bool row_ok;
+      {
+        const UnitInfo& u = sm.unit[uc & 1];
+        if (u.kind == 0) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.sched_empty[uc & 1]);
+          break;
+        }
+        const int r = t * kRows + row;
+        int q_idx = -1;
+        if (r >= u.seg_lo && r < u.seg_hi) {
+          const int qi = __ldg(&p.worklist[u.entry0 + r].x);
+          if (qi >= 0 && qi < p.seq_q) q_idx = qi;
+        }
+        row_ok = q_idx >= 0;
+        n_tiles = u.n_tiles;
+        bh = u.bh;
+        item = u.entry0 + r;
+        o_base = row_ok ? ((long long)u.bh * p.seq_q + q_idx) * 128 : 0;
+        row_end = row_ok ? (p.causal ? min(u.ctx, q_idx + 1) : u.ctx) : 0;
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.sched_empty[uc & 1]);
       ++uc;
-      if (u.kind == 0) break;
-      const int r = t * kRows + row;
-      int q_idx = -1;
-      if (r >= u.seg_lo && r < u.seg_hi) {
-        const int qi = __ldg(&p.worklist[u.entry0 + r].x);
-        if (qi >= 0 && qi < p.seq_q) q_idx = qi;
-      }
-      const bool row_ok = q_idx >= 0;
-      const long long o_base = row_ok ? ((long long)u.bh * p.seq_q + q_idx) * 128 : 0;
-      const int item = u.entry0 + r;
-      if (u.n_tiles == 0) {
-        if (row_ok) {
-          float z[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) z[i] = 0.f;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) store_row32(p.o, p.o_dtype, o_base + 32 * c, z);
-        }
+      if (n_tiles == 0) {
+        if (row_ok) store_zero_row(p.o, p.o_dtype, o_base);
         continue;
       }
-      const int row_end = row_ok ? (p.causal ? min(u.ctx, q_idx + 1) : u.ctx) : 0;
       float m = -INFINITY, l = 0.f;
       bool ab = false;
-      for (int j = 0; j < u.n_tiles; ++j) {
+      for (int j = 0; j < n_tiles; ++j) {
         const int s = kvit % kKvStages;
         if (!mbar_wait_warp(&sm.s_full[t], sc & 1, abort, p.err) ||
             !mbar_wait_warp(&sm.kv_full[s], (kvit / kKvStages) & 1, abort, p.err)) {
@@ -590,71 +748,22 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
 #pragma unroll
         for (int w = 0; w < 4; ++w) mk[w] = sm.kv_mask[s][w];
         const bool full = (mk[0] & mk[1] & mk[2] & mk[3]) == 0xFFFFFFFFu && k0 + kKeys <= row_end;
-        // ---- pass 1: tile max of the raw integer scores
-        float mx = -INFINITY, mn = INFINITY;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tc::ld32(s_col + 32 * c, v);
-          tc::ld_wait();
-          const uint32_t bits = full ? 0xFFFFFFFFu : mk[c];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float x = __uint_as_float(v[i]);
-            const bool ok = full || (((bits >> i) & 1u) && (k0 + 32 * c + i < row_end));
-            mx = ok ? fmaxf(mx, x) : mx;
-            mn = ok ? fminf(mn, x) : mn;
-            if (p.debug_scores && ok) p.debug_scores[(long long)item * p.debug_ld + k0 + 32 * c + i] = (int)x;
-          }
-        }
-        // tile max in score units (s = integer score * inv_sqrt_d)
-        const float mt = (mx == -INFINITY) ? -INFINITY : (c_scale >= 0.f ? mx * c_scale : mn * c_scale);
+        const bool warp_full = __all_sync(0xffffffffu, full);
+        if (kDebug) debug_row_scores(p, s_col, mk, k0, row_end, item);
+        // ---- pass 1: tile max of the raw integer scores, in score units
+        const float mx = warp_full ? row_tile_max<false>(s_col, mk, k0, row_end)
+                                   : row_tile_max<true>(s_col, mk, k0, row_end);
+        const float mt = (mx == -INFINITY) ? -INFINITY : mx * cabs;
         const bool need = mt > m + kTauS;
         const bool resc = need && (m != -INFINITY);
         const float alpha = resc ? ex2_approx((m - mt) * kLog2e) : 1.f;
         if (need) m = mt;
         l *= alpha;
-        if (__any_sync(0xffffffffu, resc)) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t v[32];
-            tc::ld32(o_col + 32 * c, v);
-            tc::ld_wait();
-            uint32_t a0[16], a1[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              a0[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-              a1[i] = __float_as_uint(__uint_as_float(v[16 + i]) * alpha);
-            }
-            tc::st16(o_col + 32 * c, a0);
-            tc::st16(o_col + 32 * c + 16, a1);
-          }
-          tc::st_wait();
-        }
+        if (__any_sync(0xffffffffu, resc)) rescale_row(o_col, alpha);
         // ---- pass 2: P = exp(s - m) as f16 over S's columns, l += P
         const float bias = (m == -INFINITY) ? 0.f : -m * kLog2e;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tc::ld32(s_col + 32 * c, v);
-          tc::ld_wait();
-          const uint32_t bits = full ? 0xFFFFFFFFu : mk[c];
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float pr[2];
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int ii = 2 * i + h;
-              const bool ok = full || (((bits >> ii) & 1u) && (k0 + 32 * c + ii < row_end));
-              const float e = ex2_approx(fmaf(__uint_as_float(v[ii]), k2, bias));
-              pr[h] = ok ? e : 0.f;
-              l += pr[h];
-            }
-            pk[i] = pack_f16x2(pr[0], pr[1]);
-          }
-          tc::st16(s_col + 16 * c, pk);
-        }
+        l += warp_full ? row_tile_p<false>(s_col, mk, k0, row_end, k2, bias)
+                       : row_tile_p<true>(s_col, mk, k0, row_end, k2, bias);
         tc::st_wait();
         tc::fence_before_sync();
         __syncwarp();
@@ -666,19 +775,14 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       if (!mbar_wait_warp(&sm.o_full[t], oc & 1, abort, p.err)) break;
       ++oc;
       tc::fence_after_sync();
-      const float vs = (p.v_scale_mode == 0) ? __ldg(p.v_scale) : __ldg(p.v_scale + (u.bh % p.v_scale_numel));
+      const float vs = (p.v_scale_mode == 0) ? __ldg(p.v_scale) : __ldg(p.v_scale + (bh % p.v_scale_numel));
       const float scale = 256.f * vs * ((l > 1e-6f) ? 1.f / l : 1.f);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tc::ld32(o_col + 32 * c, v);
-        tc::ld_wait();
-        if (row_ok) {
-          float f[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]) * scale;
-          store_row32(p.o, p.o_dtype, o_base + 32 * c, f);
-        }
+      if (p.o_dtype == HYPERION_DTYPE_BF16) {
+        store_o_row<HYPERION_DTYPE_BF16>(p.o, o_base, o_col, scale, row_ok);
+      } else if (p.o_dtype == HYPERION_DTYPE_F32) {
+        store_o_row<HYPERION_DTYPE_F32>(p.o, o_base, o_col, scale, row_ok);
+      } else {
+        store_o_row<HYPERION_DTYPE_F16>(p.o, o_base, o_col, scale, row_ok);
       }
       tc::fence_before_sync();
       __syncwarp();
@@ -698,12 +802,14 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
 // On failure `why` names the step.
 inline int setup(int& ctas, int& smem, const char** why) {
   smem = (int)kSmemBytes;
-  cudaError_t e = cudaFuncSetAttribute(tile_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = cudaFuncSetAttribute(tile_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tile_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) {
     *why = cudaGetErrorString(e);
     return HYPERION_ERR_CUDA;
   }
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, tile_fwd_kernel, kThreads, smem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, tile_fwd_kernel<false>, kThreads, smem);
   if (e != cudaSuccess) {
     *why = cudaGetErrorString(e);
     return HYPERION_ERR_CUDA;
@@ -720,7 +826,11 @@ inline int launch(const FwdParams& p, int n_sm, int ctas, int smem, cudaStream_t
   const int n_chunks = (p.total_work + kChunk - 1) / kChunk;
   const int grid = std::min(n_chunks, n_sm * std::max(ctas, 1));
   if (grid <= 0) return HYPERION_OK;
-  tile_fwd_kernel<<<grid, kThreads, smem, st>>>(p);
+  if (p.debug_scores) {
+    tile_fwd_kernel<true><<<grid, kThreads, smem, st>>>(p);
+  } else {
+    tile_fwd_kernel<false><<<grid, kThreads, smem, st>>>(p);
+  }
   if (grid_out) *grid_out = grid;
   return HYPERION_OK;
 }
