@@ -227,6 +227,9 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   p.num_blocks = num_blocks;
   p.inv_sqrt_d = inv_sqrt_d;
   p.causal = causal ? 1 : 0;
+  // Contiguous layout: page ids are bh * num_blocks + page; all of them are in the
+  // pool when the pool holds n_bh * num_blocks pages.
+  p.pages_all_valid = (!paged && (long long)ext->n_bh * num_blocks <= p.pool_blocks) ? 1 : 0;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.counters = reinterpret_cast<uint32_t*>(ws + hyp::kWsCounters);
   p.err = reinterpret_cast<uint32_t*>(ws + hyp::kWsError);

@@ -54,6 +54,7 @@ struct FwdParams {
   int n_split;
   int* debug_scores;
   long long debug_ld;
+  int pages_all_valid;  // 1: every page id the kernels can read is inside the pool (host-checked)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -3,9 +3,8 @@
 // One CTA per SM, persistent.  A unit of work is a chunk of 256 consecutive work
 // items (two 128-row Q tiles) of one (batch, head) row `bh`; chunks are taken
 // with an atomic ticket in the caller's workspace (the reference's g_work_counter
-// work stealing, hyperion_fa3_production_final.py:236-243, :332-336), the last
-// chunks first so that, for causal prefill in (bh, q) order, the longest rows go
-// out first.  For every 128-key tile of the unit's KV range:
+// work stealing, hyperion_fa3_production_final.py:236-243, :332-336), longest
+// causal rows first.  The unit's keys are walked in 128-key tiles:
 //
 //   loader warp    cp.async.bulk of the raw page pieces (sign bits 16 B/key, FP8
 //                  codes 128 B/key) into a 3-stage ring, with the key-valid mask
@@ -16,19 +15,20 @@
 //                  layout; Q rows of the unit likewise, once per unit;
 //   MMA warp       S_t = Q_t K^T as a kind::f8f6f4 tcgen05.mma (the +-1 products
 //                  sum to D - 2*popcount(q XOR k) exactly in the f32 accumulator,
-//                  README.md:22), then O_t += P_t V as a kind::f16 MMA with P read
-//                  from TMEM; tcgen05.commit hands each result to its consumer;
+//                  README.md:22), then O_t += P_t V, a kind::f16 MMA with P read
+//                  from TMEM; tcgen05.commit hands each result on;
 //   softmax WG t   (4 warps per Q tile, one thread per row = TMEM lane) reads S,
 //                  applies the masks (causal: key > q_idx, :483-486), keeps the
-//                  running max with the reference's online update (:544-572)
-//                  rescaling O in TMEM only when the max grows by more than
-//                  2^8, writes P as f16 back into TMEM over S, and at the end
-//                  of the unit finalises O = acc * (l > 1e-6 ? 1/l : 1) (:582-593).
+//                  running max with the reference's online update (:544-572),
+//                  writes P as f16 over S, and at the end of the unit finalises
+//                  O = acc * (l > 1e-6 ? 1/l : 1) (:582-593).  The two warpgroups
+//                  take turns for their exponential passes (ping-pong), so one
+//                  runs while the tensor core serves the other's MMAs.
 //
-// TMEM (512 columns): tile t uses S/P at [256t, 256t+128) and O at [256t+128, 256t+256).
-// Every mbarrier wait is bounded; on a timeout the CTA raises
-// HYPERION_DEVERR_WAIT_TIMEOUT, lets in-flight copies and MMAs land, frees TMEM
-// and exits.
+// TMEM (512 columns): Q tile t owns S/P at [256t, 256t+128) and O at
+// [256t+128, 256t+256).  Every mbarrier wait is bounded; on a timeout the CTA
+// raises HYPERION_DEVERR_WAIT_TIMEOUT, lets in-flight copies and MMAs land,
+// frees TMEM and exits.
 #pragma once
 
 #include "common.cuh"
@@ -40,7 +40,7 @@ namespace tile {
 constexpr int kRows = 128;
 constexpr int kQTiles = 2;
 constexpr int kChunk = kRows * kQTiles;
-constexpr int kKeys = 128;
+constexpr int kKeys = 128;  // keys per KV tile
 constexpr int kRawStages = 3;
 constexpr int kKvStages = 2;
 constexpr int kMmaWarp = 8;
@@ -50,6 +50,9 @@ constexpr int kConvWarps = 4;
 constexpr int kThreads = 32 * (kConvWarp0 + kConvWarps);  // 448
 constexpr int kSchedConsumers = 4 * kQTiles + 1 + kConvWarps;  // warps that read each unit
 constexpr uint32_t kTmemCols = 512;
+constexpr int kKTileBytes = kKeys * 128;      // e4m3 +-1, K-major SW128
+constexpr int kVTileBytes = kKeys * 256;      // f16, MN-major SW128: two 64-dim blocks
+constexpr int kVBlockBytes = kKeys * 128;     // one 64-dim block (LBO of the V descriptor)
 // Lazy rescale threshold: P = exp(s - m) may grow to 2^8 before the running max
 // is moved (8 / log2(e) in score units), well inside the f16 range of P.
 constexpr float kTauS = 5.545177444479562f;
@@ -69,8 +72,8 @@ struct UnitInfo {
 
 struct Smem {
   alignas(1024) uint8_t q[kQTiles][kRows * 128];
-  alignas(1024) uint8_t kt[kKvStages][kKeys * 128];
-  alignas(1024) uint8_t vt[kKvStages][kKeys * 256];
+  alignas(1024) uint8_t kt[kKvStages][kKTileBytes];
+  alignas(1024) uint8_t vt[kKvStages][kVTileBytes];
   alignas(128) uint8_t raw_k[kRawStages][kKeys * 16];
   alignas(128) uint8_t raw_v[kRawStages][kKeys * 128];
   uint32_t raw_mask[kRawStages][4];
@@ -88,6 +91,7 @@ struct Smem {
   alignas(8) uint64_t p_full[kQTiles];
   alignas(8) uint64_t o_full[kQTiles];
   alignas(8) uint64_t o_empty[kQTiles];
+  alignas(8) uint64_t turn[kQTiles];  // softmax ping-pong: warpgroup t may run its P pass
   alignas(8) uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -198,93 +202,117 @@ __device__ __forceinline__ void store_zero_row(void* o, int dtype, long long o_b
   }
 }
 
-// Mask bits of chunk c (keys kbase + 32c .. +31) for a row whose keys end at row_end.
-__device__ __forceinline__ uint32_t chunk_bits(const uint32_t (&mk)[4], int c, int kbase, int row_end) {
-  const int lim = row_end - kbase - 32 * c;
-  const uint32_t lm = lim >= 32 ? 0xFFFFFFFFu : (lim <= 0 ? 0u : ((1u << lim) - 1u));
-  return mk[c] & lm;
+// Valid-key bits of 16-key chunk h (keys kbase + 16h ..) for a row whose keys end at row_end.
+__device__ __forceinline__ uint32_t chunk_bits(const uint32_t (&mk)[4], int h, int kbase, int row_end) {
+  const int lim = row_end - kbase - 16 * h;
+  const uint32_t lm = lim >= 16 ? 0xFFFFu : (lim <= 0 ? 0u : ((1u << lim) - 1u));
+  return (mk[h >> 1] >> (16 * (h & 1))) & lm;
 }
 
-// Max of this thread's row over the 128 S columns of the tile (raw integer scores).
+// Max of this thread's row over the 128 S columns of the tile (raw integer scores),
+// two 16-column loads in flight per wait.
 template <bool kMasked>
 __device__ __forceinline__ float row_tile_max(uint32_t s_col, const uint32_t (&mk)[4], int kbase, int row_end) {
   float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
-#pragma unroll 2
-  for (int h = 0; h < 8; ++h) {
-    uint32_t v[16];
-    tc::ld16(s_col + 16 * h, v);
-    tc::ld_wait();
-    const uint32_t bits = kMasked ? (chunk_bits(mk, h >> 1, kbase, row_end) >> (16 * (h & 1))) : 0xFFFFu;
+#pragma unroll 1
+  for (int h = 0; h < 8; h += 2) {
+    uint32_t va[16], vb[16];
+    tc::ld16(s_col + 16 * h, va);
+    tc::ld16(s_col + 16 * (h + 1), vb);
+    tc::ld_wait_regs(va);
+    tc::ld_wait_regs(vb);
 #pragma unroll
-    for (int i = 0; i < 16; i += 4) {
-      float x0 = __uint_as_float(v[i]), x1 = __uint_as_float(v[i + 1]);
-      float x2 = __uint_as_float(v[i + 2]), x3 = __uint_as_float(v[i + 3]);
-      if (kMasked) {
-        x0 = ((bits >> i) & 1u) ? x0 : -INFINITY;
-        x1 = ((bits >> (i + 1)) & 1u) ? x1 : -INFINITY;
-        x2 = ((bits >> (i + 2)) & 1u) ? x2 : -INFINITY;
-        x3 = ((bits >> (i + 3)) & 1u) ? x3 : -INFINITY;
+    for (int q = 0; q < 2; ++q) {
+      const uint32_t(&v)[16] = q ? vb : va;
+      const uint32_t bits = kMasked ? chunk_bits(mk, h + q, kbase, row_end) : 0xFFFFu;
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) {
+        float x0 = __uint_as_float(v[i]), x1 = __uint_as_float(v[i + 1]);
+        float x2 = __uint_as_float(v[i + 2]), x3 = __uint_as_float(v[i + 3]);
+        if (kMasked) {
+          x0 = ((bits >> i) & 1u) ? x0 : -INFINITY;
+          x1 = ((bits >> (i + 1)) & 1u) ? x1 : -INFINITY;
+          x2 = ((bits >> (i + 2)) & 1u) ? x2 : -INFINITY;
+          x3 = ((bits >> (i + 3)) & 1u) ? x3 : -INFINITY;
+        }
+        a0 = fmaxf(a0, x0);
+        a1 = fmaxf(a1, x1);
+        a2 = fmaxf(a2, x2);
+        a3 = fmaxf(a3, x3);
       }
-      a0 = fmaxf(a0, x0);
-      a1 = fmaxf(a1, x1);
-      a2 = fmaxf(a2, x2);
-      a3 = fmaxf(a3, x3);
     }
   }
   return fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
 }
 
-// P = 2^(S*k2 + bias) for this thread's row, packed to f16 pairs and stored over
-// the first 64 columns of S (the P of columns [16h, 16h+16) lands on columns
-// [8h, 8h+8), already read); returns the sum of P.
-template <bool kMasked>
-__device__ __forceinline__ float row_tile_p(uint32_t s_col, const uint32_t (&mk)[4], int kbase, int row_end,
-                                            float k2, float bias) {
-  float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
-#pragma unroll 2
-  for (int h = 0; h < 8; ++h) {
-    uint32_t v[16];
-    tc::ld16(s_col + 16 * h, v);
-    tc::ld_wait();
-    const uint32_t bits = kMasked ? (chunk_bits(mk, h >> 1, kbase, row_end) >> (16 * (h & 1))) : 0xFFFFu;
-    uint32_t pk[8];
+// Exponentials 2^(v*k2 + bias) of one 16-column chunk.
+__device__ __forceinline__ void p_exp16(const uint32_t (&v)[16], float k2, float bias, float (&e)[16]) {
 #pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-      float e0 = ex2_approx(fmaf(__uint_as_float(v[2 * i]), k2, bias));
-      float e1 = ex2_approx(fmaf(__uint_as_float(v[2 * i + 1]), k2, bias));
-      float e2 = ex2_approx(fmaf(__uint_as_float(v[2 * i + 2]), k2, bias));
-      float e3 = ex2_approx(fmaf(__uint_as_float(v[2 * i + 3]), k2, bias));
-      if (kMasked) {
-        e0 = ((bits >> (2 * i)) & 1u) ? e0 : 0.f;
-        e1 = ((bits >> (2 * i + 1)) & 1u) ? e1 : 0.f;
-        e2 = ((bits >> (2 * i + 2)) & 1u) ? e2 : 0.f;
-        e3 = ((bits >> (2 * i + 3)) & 1u) ? e3 : 0.f;
-      }
-      l0 += e0;
-      l1 += e1;
-      l2 += e2;
-      l3 += e3;
-      pk[i] = pack_f16x2(e0, e1);
-      pk[i + 1] = pack_f16x2(e2, e3);
+  for (int i = 0; i < 16; ++i) e[i] = ex2_approx(fmaf(__uint_as_float(v[i]), k2, bias));
+}
+
+// Finishes chunk h (exponentials in `e`: mask, add to l[], pack to f16 pairs, store
+// over columns [8h, 8h+8) of S) while computing the exponentials of the next chunk
+// (`vn` -> `en`) pair by pair: the exponential unit takes one warp instruction per
+// 8 cycles, and the finishing work of chunk h fills the issue slots in between.
+template <bool kMasked, bool kNext>
+__device__ __forceinline__ void p_step(uint32_t s_col, int h, float (&e)[16], uint32_t bits, const uint32_t (&vn)[16],
+                                       float (&en)[16], float k2, float bias, float (&l)[4]) {
+  uint32_t pk[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (kNext) {
+      en[2 * i] = ex2_approx(fmaf(__uint_as_float(vn[2 * i]), k2, bias));
+      en[2 * i + 1] = ex2_approx(fmaf(__uint_as_float(vn[2 * i + 1]), k2, bias));
     }
-    tc::st8(s_col + 8 * h, pk);
+    float e0 = e[2 * i], e1 = e[2 * i + 1];
+    if (kMasked) {
+      e0 = ((bits >> (2 * i)) & 1u) ? e0 : 0.f;
+      e1 = ((bits >> (2 * i + 1)) & 1u) ? e1 : 0.f;
+    }
+    l[i & 3] += e0 + e1;
+    pk[i] = pack_f16x2(e0, e1);
   }
-  return (l0 + l1) + (l2 + l3);
+  tc::st8(s_col + 8 * h, pk);
+}
+
+// P = 2^(S*k2 + bias) for this thread's row over the 128-key tile; returns sum(P).
+// While chunk h is finished, the exponentials of chunk h+1 run and the TMEM load of
+// chunk h+2 is in flight.
+template <bool kMasked>
+__device__ __forceinline__ float row_tile_p(uint32_t s_col, const uint32_t (&mk)[4], int kbase, int row_end, float k2,
+                                           float bias) {
+  float l[4] = {0.f, 0.f, 0.f, 0.f};
+  uint32_t va[16], vb[16];
+  float ea[16], eb[16];
+  tc::ld16(s_col, va);
+  tc::ld16(s_col + 16, vb);
+  tc::ld_wait_regs(va);
+  tc::ld_wait_regs(vb);
+  p_exp16(va, k2, bias, ea);
+#pragma unroll 1
+  for (int h = 0; h < 6; h += 2) {
+    // va is free (chunk h's exponentials are in ea): load chunk h+2 into it.
+    tc::ld16(s_col + 16 * (h + 2), va);
+    p_step<kMasked, true>(s_col, h, ea, kMasked ? chunk_bits(mk, h, kbase, row_end) : 0xFFFFu, vb, eb, k2, bias, l);
+    tc::ld_wait_regs(va);
+    tc::ld16(s_col + 16 * (h + 3), vb);
+    p_step<kMasked, true>(s_col, h + 1, eb, kMasked ? chunk_bits(mk, h + 1, kbase, row_end) : 0xFFFFu, va, ea, k2, bias,
+                          l);
+    tc::ld_wait_regs(vb);
+  }
+  p_step<kMasked, true>(s_col, 6, ea, kMasked ? chunk_bits(mk, 6, kbase, row_end) : 0xFFFFu, vb, eb, k2, bias, l);
+  p_step<kMasked, false>(s_col, 7, eb, kMasked ? chunk_bits(mk, 7, kbase, row_end) : 0xFFFFu, va, ea, k2, bias, l);
+  return (l[0] + l[1]) + (l[2] + l[3]);
 }
 
 // O row *= alpha (lanes that need no rescale pass alpha = 1).
 __device__ __forceinline__ void rescale_row(uint32_t o_col, float alpha) {
-#pragma unroll
+#pragma unroll 1
   for (int c = 0; c < 8; ++c) {
     uint32_t v[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(o_col + 16 * c)
-        : "memory");
-    tc::ld_wait();
+    tc::ld16(o_col + 16 * c, v);
+    tc::ld_wait_regs(v);
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
     tc::st16(o_col + 16 * c, v);
@@ -297,16 +325,16 @@ __device__ __noinline__ void debug_row_scores(const FwdParams& p, uint32_t s_col
                                               int row_end, int item) {
   const bool flip = p.inv_sqrt_d < 0.f;
 #pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
-    uint32_t v[32];
-    tc::ld32(s_col + 32 * c, v);
-    tc::ld_wait();
-    const uint32_t bits = chunk_bits(mk, c, kbase, row_end);
+  for (int h = 0; h < 8; ++h) {
+    uint32_t v[16];
+    tc::ld16(s_col + 16 * h, v);
+    tc::ld_wait_regs(v);
+    const uint32_t bits = chunk_bits(mk, h, kbase, row_end);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < 16; ++i) {
       if ((bits >> i) & 1u) {
         const int x = (int)__uint_as_float(v[i]);
-        p.debug_scores[(long long)item * p.debug_ld + kbase + 32 * c + i] = flip ? -x : x;
+        p.debug_scores[(long long)item * p.debug_ld + kbase + 16 * h + i] = flip ? -x : x;
       }
     }
   }
@@ -341,6 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       mbar_init(&sm.p_full[t], 4);
       mbar_init(&sm.o_full[t], 1);
       mbar_init(&sm.o_empty[t], 4);
+      mbar_init(&sm.turn[t], 4);
     }
     mbar_init(&sm.drain, 1);
     sm.abort = 0;
@@ -533,7 +562,8 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       ++uc;
       if (u.kind == 0) break;
       if (u.n_tiles == 0) continue;
-      // ---- Q rows of the unit -> e4m3 +-1, K-major SW128
+      // ---- Q rows of the unit -> e4m3 +-1, K-major SW128 (a negative inv_sqrt_d is
+      // folded in by flipping every bit: the scores change sign)
       if (!mbar_wait_warp(&sm.q_empty, (uq & 1) ^ 1, abort, p.err)) break;
 #pragma unroll
       for (int i = 0; i < kQTiles; ++i) {
@@ -565,7 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           ab = true;
           break;
         }
-        // K: thread ct owns key ct.
+        // K: thread ct owns key ct (16 bytes of sign bits -> 128 e4m3 bytes).
         {
           const uint4 kb = *reinterpret_cast<const uint4*>(&sm.raw_k[r][ct * 16]);
           const uint32_t words[4] = {kb.x, kb.y, kb.z, kb.w};
@@ -574,19 +604,28 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           for (int c = 0; c < 8; ++c)
             st_shared_v4(tb + sw128_off(ct, c), expand16((words[c >> 1] >> (16 * (c & 1))) & 0xFFFFu));
         }
-        // V: 2048 (key, 8-dim chunk) tasks, 16 per thread; 16 lanes cover one key row.
+        // V: 2048 (key, 8-dim chunk) tasks, 16 per thread in two batches of 8 loads;
+        // 16 lanes cover one key row.
         {
           const uint32_t vb = smem_u32(&sm.vt[s][0]);
-#pragma unroll 4
-          for (int i = 0; i < 16; ++i) {
-            const int task = ct + 128 * i;
-            const int key = task >> 4;
-            const int c8 = task & 15;
-            const uint2 w = *reinterpret_cast<const uint2*>(&sm.raw_v[r][key * 128 + c8 * 8]);
-            uint4 o;
-            fp8x4_to_f16x4(w.x, o.x, o.y);
-            fp8x4_to_f16x4(w.y, o.z, o.w);
-            st_shared_v4(vb + (c8 >> 3) * 16384u + sw128_off(key, c8 & 7), o);
+#pragma unroll 1
+          for (int half = 0; half < 2; ++half) {
+            uint2 w[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int task = ct + 128 * (8 * half + i);
+              w[i] = *reinterpret_cast<const uint2*>(&sm.raw_v[r][(task >> 4) * 128 + (task & 15) * 8]);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int task = ct + 128 * (8 * half + i);
+              const int key = task >> 4;
+              const int c8 = task & 15;
+              uint4 o;
+              fp8x4_to_f16x4(w[i].x, o.x, o.y);
+              fp8x4_to_f16x4(w[i].y, o.z, o.w);
+              st_shared_v4(vb + (c8 >> 3) * (uint32_t)kVBlockBytes + sw128_off(key, c8 & 7), o);
+            }
           }
         }
         if (ct < 4) sm.kv_mask[s][ct] = sm.raw_mask[r][ct];
@@ -603,30 +642,35 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     }
   } else if (warp == kMmaWarp) {
     // ================================================================ MMA issuer
+    // One thread issues every MMA and commit (a tcgen05.commit tracks the MMAs of
+    // the thread that issues it); QK with N = 128 and PV with N = 128 keep each
+    // instruction at the tensor core's full per-instruction rate.
     if (lane == 0) {
       uint32_t uc = 0, kvit = 0, uq = 0, uo = 0;
       uint32_t pc[kQTiles] = {0u, 0u};
       const uint32_t q_base = smem_u32(&sm.q[0][0]);
       const uint32_t k_base = smem_u32(&sm.kt[0][0]);
       const uint32_t v_base = smem_u32(&sm.vt[0][0]);
+      const uint64_t q_desc = tc::sw128_desc(q_base, 16, 1024);
+      const uint64_t k_desc = tc::sw128_desc(k_base, 16, 1024);
+      const uint64_t v_desc = tc::sw128_desc(v_base, kVBlockBytes, 1024);
       bool ab = false;
+      // S_t = Q_t K(stage s)^T  (M 128, N 128, K 128 in 4 steps of 32 bytes)
       auto qk = [&](int t, int s) {
         const uint32_t d = tmem + (uint32_t)(t * 256);
+        const uint64_t ad = q_desc + (uint64_t)(t * (kRows * 128) / 16);
+        const uint64_t bd = k_desc + (uint64_t)(s * kKTileBytes / 16);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad = tc::sw128_desc(q_base + t * (kRows * 128) + kk * 32, 16, 1024);
-          const uint64_t bd = tc::sw128_desc(k_base + s * (kKeys * 128) + kk * 32, 16, 1024);
-          tc::mma_f8f6f4_ss(d, ad, bd, tc::kIdescQK, kk > 0 ? 1u : 0u);
-        }
+        for (int kk = 0; kk < 4; ++kk) tc::mma_f8f6f4_ss(d, ad + 2 * kk, bd + 2 * kk, tc::kIdescQK, kk > 0 ? 1u : 0u);
       };
+      // O_t (+)= P_t V(stage s)  (M 128, N 128, K 128 keys in 8 steps of 16)
       auto pv = [&](int t, int s, bool acc) {
         const uint32_t d = tmem + (uint32_t)(t * 256 + 128);
         const uint32_t a = tmem + (uint32_t)(t * 256);
+        const uint64_t bd = v_desc + (uint64_t)(s * kVTileBytes / 16);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t bd = tc::sw128_desc(v_base + s * (kKeys * 256) + kk * 2048, 16384, 1024);
-          tc::mma_f16_ts(d, a + kk * 8, bd, tc::kIdescPV, (acc || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < 8; ++kk)
+          tc::mma_f16_ts(d, a + kk * 8, bd + 128 * kk, tc::kIdescPV, (acc || kk > 0) ? 1u : 0u);
       };
       for (;;) {
         if (!mbar_wait(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) break;
@@ -650,19 +694,18 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           s = (kvit + j) % kKvStages;
           const uint32_t nxt = kvit + j + 1;
           for (int t = 0; t < kQTiles; ++t) {
-            if (!mbar_wait(&sm.p_full[t], pc[t] & 1, abort, p.err)) {
+            if (!mbar_wait(&sm.p_full[t], pc[t] & 1, abort, p.err) ||
+                (j == 0 && !mbar_wait(&sm.o_empty[t], (uo & 1) ^ 1, abort, p.err))) {
               ab = true;
               break;
             }
             ++pc[t];
-            if (j == 0 && !mbar_wait(&sm.o_empty[t], (uo & 1) ^ 1, abort, p.err)) {
-              ab = true;
-              break;
-            }
             tc::fence_after_sync();
             pv(t, s, j > 0);
             if (j == n - 1) tc::commit(&sm.o_full[t]);
             if (t == kQTiles - 1) tc::commit(&sm.kv_empty[s]);
+            // The QK of the next tile reuses this Q tile's S/P columns: it is issued
+            // after the PV that reads P (tcgen05 MMAs of one thread run in order).
             if (j + 1 < n) {
               const int s2 = nxt % kKvStages;
               if (t == 0) {
@@ -699,6 +742,9 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     // tile scores here are always multiplied by |inv_sqrt_d| and their max is a max.
     const float cabs = fabsf(p.inv_sqrt_d);
     const float k2 = cabs * kLog2e;
+    // Running max from which on a row needs no max pass: (head_dim * |inv_sqrt_d|)
+    // minus 11, so exp(s - m) <= e^11 < 2^15.9 for every possible score s.
+    const float m_safe = 128.f * cabs - 11.0f;
     uint32_t uc = 0, kvit = 0, sc = 0, oc = 0;
     for (;;) {
       if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) break;
@@ -735,39 +781,63 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       float m = -INFINITY, l = 0.f;
       bool ab = false;
       for (int j = 0; j < n_tiles; ++j) {
-        const int s = kvit % kKvStages;
-        if (!mbar_wait_warp(&sm.s_full[t], sc & 1, abort, p.err) ||
-            !mbar_wait_warp(&sm.kv_full[s], (kvit / kKvStages) & 1, abort, p.err)) {
+        const uint32_t g = kvit;
+        const int s = g % kKvStages;
+        if (!mbar_wait_warp(&sm.s_full[t], sc & 1, abort, p.err)) {
           ab = true;
           break;
         }
         ++sc;
+        uint32_t mk[4] = {0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu};
+        if (!p.pages_all_valid) {
+          // Page ids can fall outside the pool: read the tile's key mask (the
+          // converters copied it before completing this phase of kv_full).
+          if (!mbar_wait_warp(&sm.kv_full[s], (g / kKvStages) & 1, abort, p.err)) {
+            ab = true;
+            break;
+          }
+#pragma unroll
+          for (int w = 0; w < 4; ++w) mk[w] = sm.kv_mask[s][w];
+        }
         tc::fence_after_sync();
         const int k0 = j * kKeys;
-        uint32_t mk[4];
-#pragma unroll
-        for (int w = 0; w < 4; ++w) mk[w] = sm.kv_mask[s][w];
         const bool full = (mk[0] & mk[1] & mk[2] & mk[3]) == 0xFFFFFFFFu && k0 + kKeys <= row_end;
         const bool warp_full = __all_sync(0xffffffffu, full);
         if (kDebug) debug_row_scores(p, s_col, mk, k0, row_end, item);
-        // ---- pass 1: tile max of the raw integer scores, in score units
-        const float mx = warp_full ? row_tile_max<false>(s_col, mk, k0, row_end)
-                                   : row_tile_max<true>(s_col, mk, k0, row_end);
-        const float mt = (mx == -INFINITY) ? -INFINITY : mx * cabs;
-        const bool need = mt > m + kTauS;
-        const bool resc = need && (m != -INFINITY);
-        const float alpha = resc ? ex2_approx((m - mt) * kLog2e) : 1.f;
-        if (need) m = mt;
-        l *= alpha;
-        if (__any_sync(0xffffffffu, resc)) rescale_row(o_col, alpha);
-        // ---- pass 2: P = exp(s - m) as f16 over S's columns, l += P
+        if (!__all_sync(0xffffffffu, m >= m_safe)) {
+          // ---- max pass (first tiles of a row, or scores too large for a fixed m).
+          // S(j) ready implies the PV of tile j-1 is done (it was issued before the
+          // QK of tile j), so O may be rescaled here.
+          const float mx = warp_full ? row_tile_max<false>(s_col, mk, k0, row_end)
+                                     : row_tile_max<true>(s_col, mk, k0, row_end);
+          const float mt = (mx == -INFINITY) ? -INFINITY : mx * cabs;
+          const bool need = mt > m + kTauS;
+          const bool resc = need && (m != -INFINITY);
+          const float alpha = resc ? ex2_approx((m - mt) * kLog2e) : 1.f;
+          if (need) m = mt;
+          l *= alpha;
+          if (__any_sync(0xffffffffu, resc)) rescale_row(o_col, alpha);
+        }
+        // ---- P pass, one warpgroup at a time: the two Q tiles take turns so each P
+        // pass has the SM's exponential units to itself while the tensor core runs
+        // the other tile's MMAs.  Turn g of warpgroup 0 follows turn g-1 of
+        // warpgroup 1, turn g of warpgroup 1 follows turn g of warpgroup 0.
+        if (!mbar_wait_warp(&sm.turn[t], t == 0 ? ((g & 1) ^ 1) : (g & 1), abort, p.err)) {
+          ab = true;
+          break;
+        }
+        // Once m >= m_safe every score is <= head_dim * |inv_sqrt_d| <= m + 11, so
+        // P <= 2^15.9 fits f16 and the running max never has to move again.
         const float bias = (m == -INFINITY) ? 0.f : -m * kLog2e;
         l += warp_full ? row_tile_p<false>(s_col, mk, k0, row_end, k2, bias)
                        : row_tile_p<true>(s_col, mk, k0, row_end, k2, bias);
         tc::st_wait();
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.p_full[t]);
+        if (lane == 0) {
+          mbar_arrive(&sm.turn[t ^ 1]);
+          mbar_arrive(&sm.p_full[t]);
+        }
         ++kvit;
       }
       if (ab) break;
