@@ -342,3 +342,73 @@ int hyperion_read_device_errors(void* workspace, size_t workspace_bytes, void* s
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// The forward for callers that cannot allocate device memory.
+//
+// Its scratch (work counter at +0, error word at +64, split-KV partials from +256,
+// the same layout as a caller workspace) is this file-scope array: one copy per
+// device, created when the library's device code is loaded there and kept until
+// the process exits.  Host code may not use the array's name as a device address
+// (on the host it names a stand-in object), so each device's address is looked up
+// once with cudaGetSymbolAddress and cached.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[HYPERION_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+void* g_noalloc_addr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// Device address of the current device's copy of g_noalloc_scratch.
+int noalloc_scratch(uint8_t** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(HYPERION_ERR_UNSUPPORTED, "device ordinal out of range");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    if (ptr == nullptr || reinterpret_cast<uintptr_t>(ptr) % 256 != 0)
+      return fail(HYPERION_ERR_CUDA, "scratch array has no 256-byte aligned device address");
+    g_noalloc_addr[dev] = ptr;
+  }
+  *out = static_cast<uint8_t*>(g_noalloc_addr[dev]);
+  return HYPERION_OK;
+}
+
+}  // namespace
+
+extern "C" int hyperion_apex_kernel_noalloc(const int32_t* worklist, int32_t total_work, const uint32_t* Q,
+                                            const float* Q_scale, const uint32_t* K_cache, const float* K_scale,
+                                            const uint8_t* V_cache, const float* V_scale,
+                                            const int32_t* context_lens, const int32_t* block_tables, void* O,
+                                            int32_t seq_q, int32_t head_dim, int32_t k_packed_bytes,
+                                            int32_t block_size, int32_t num_blocks, float inv_sqrt_d,
+                                            int32_t causal, const hyperion_extents* ext, void* stream) {
+  uint8_t* scratch = nullptr;
+  const int rc0 = noalloc_scratch(&scratch);
+  if (rc0) return rc0;
+  // The forward zeroes the work counter on `stream` before its kernels, and
+  // rejects a call whose split-KV partials exceed the bytes it is given.
+  const int rc = hyperion_apex_kernel_ex(worklist, total_work, Q, Q_scale, K_cache, K_scale, V_cache, V_scale,
+                                         context_lens, block_tables, O, seq_q, head_dim, k_packed_bytes, block_size,
+                                         num_blocks, inv_sqrt_d, causal, ext, nullptr, scratch,
+                                         HYPERION_NOALLOC_SCRATCH_BYTES, stream);
+  if (rc == HYPERION_ERR_WORKSPACE) {
+    const DevInfo* di = nullptr;
+    if (get_dev(&di) != HYPERION_OK) return rc;
+    const long long max_keys = (long long)block_size * num_blocks;
+    const int ns = choose_splits(*di, head_dim, total_work, max_keys);
+    char msg[320];
+    std::snprintf(msg, sizeof(msg),
+                  "hyperion_apex_kernel_noalloc: this call needs %zu bytes of scratch (%d work items x %d KV splits "
+                  "of %d floats), more than its fixed %zu bytes; pass fewer work items per call or use "
+                  "hyperion_apex_kernel with a workspace",
+                  (size_t)hyp::kWsPartials + partial_bytes(total_work, ns, head_dim), (int)total_work, ns,
+                  2 + (int)head_dim, (size_t)HYPERION_NOALLOC_SCRATCH_BYTES);
+    g_last_error = msg;
+  }
+  return rc;
+}

@@ -44,7 +44,11 @@ EXPORTED = (
     "hyperion_last_call_info",
     "hyperion_last_error_string",
     "hyperion_version",
+    "hyperion_apex_kernel_noalloc",
 )
+
+# Fixed per-device scratch of hyperion_apex_kernel_noalloc (HYPERION_NOALLOC_SCRATCH_BYTES).
+NOALLOC_SCRATCH_BYTES = 32 << 20
 
 
 class Extents(ctypes.Structure):
@@ -109,6 +113,8 @@ def _load() -> ctypes.CDLL:
     lib.hyperion_last_error_string.argtypes = []
     lib.hyperion_version.restype = _i32
     lib.hyperion_version.argtypes = []
+    lib.hyperion_apex_kernel_noalloc.restype = ctypes.c_int
+    lib.hyperion_apex_kernel_noalloc.argtypes = _FWD_ARGS + [_vp]
     return lib
 
 

@@ -158,6 +158,38 @@ const char* hyperion_last_error_string(void);
 /* Library version as major*10000 + minor*100 + patch. */
 int32_t hyperion_version(void);
 
+/* Fixed scratch of hyperion_apex_kernel_noalloc, per device, in bytes. */
+#define HYPERION_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+
+/* The forward without a caller workspace.  It has no counterpart in the reference.
+ *
+ * Some callers cannot allocate device memory.  Examples are a plugin whose host
+ * framework owns the device allocator, an engine that reserves all memory at start-up,
+ * and a binding with no allocator of its own.  For them, this entry point keeps the
+ * forward's scratch (work counter, error word and split-KV partials) in a fixed array
+ * of HYPERION_NOALLOC_SCRATCH_BYTES that the library holds on every device where its
+ * device code is loaded, until the process exits.  It calls no cudaMalloc or cudaFree.
+ * The caller passes the inputs and O exactly as for hyperion_apex_kernel.
+ *
+ * - The first call on a device looks up that device's copy of the array, with the
+ *   device current.  Make that first call before any stream capture.
+ * - A call whose split-KV partials do not fit in the array returns
+ *   HYPERION_ERR_WORKSPACE, with the bytes it needed in hyperion_last_error_string().
+ *   Smaller worklists per call, or hyperion_apex_kernel, avoid that.
+ * - Every call on a device shares the one array.  The work counter is zeroed on
+ *   `stream` at the start of each call.  Two calls that overlap on the same GPU (two
+ *   streams, or two host threads) race on the array: order them on one stream.
+ * - Device-side error flags are kept in the array and are not readable through
+ *   this entry point. */
+int hyperion_apex_kernel_noalloc(const int32_t* worklist, int32_t total_work,
+                                 const uint32_t* Q, const float* Q_scale,
+                                 const uint32_t* K_cache, const float* K_scale,
+                                 const uint8_t* V_cache, const float* V_scale,
+                                 const int32_t* context_lens, const int32_t* block_tables,
+                                 void* O, int32_t seq_q, int32_t head_dim, int32_t k_packed_bytes,
+                                 int32_t block_size, int32_t num_blocks, float inv_sqrt_d,
+                                 int32_t causal, const hyperion_extents* ext, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
