@@ -204,6 +204,29 @@ __device__ __forceinline__ uint32_t fp8x2_even_to_f16x2_div256(uint32_t v) {
   return ((v << 7) & 0x3F803F80u) | ((v << 8) & 0x80008000u);
 }
 
+// {a, b} -> f16x2 (a in the low half), round to nearest even.
+__device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %2, %1;" : "=r"(r) : "f"(a), "f"(b));
+  return r;
+}
+// a * b + c on f16x2 operands, round to nearest even.
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+__device__ __forceinline__ float f16_lo_to_f32(uint32_t v) {
+  float r;
+  asm("{.reg .b16 l, h; mov.b32 {l, h}, %1; cvt.f32.f16 %0, l;}" : "=f"(r) : "r"(v));
+  return r;
+}
+__device__ __forceinline__ float f16_hi_to_f32(uint32_t v) {
+  float r;
+  asm("{.reg .b16 l, h; mov.b32 {l, h}, %1; cvt.f32.f16 %0, h;}" : "=f"(r) : "r"(v));
+  return r;
+}
+
 // Integer score D - 2*popcount(q XOR k) over W 32-bit words.
 template <int W>
 __device__ __forceinline__ int sign_score(const uint32_t (&q)[W], const uint32_t* k) {

@@ -96,6 +96,8 @@ template <int D>
 __global__ void __launch_bounds__(kThreads, 5) row_fwd_kernel(FwdParams p, int total_units) {
   constexpr int W = D / 32;
   constexpr int DPL = D / 32;  // dims per lane
+  constexpr int NW = DPL / 4;  // 32-bit words of V bytes per lane and key
+  static_assert(D == 128 || D == 256, "row kernel: head_dim 128 or 256");
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem<D>& sm = *reinterpret_cast<Smem<D>*>(smem_raw);
 
@@ -277,25 +279,57 @@ __global__ void __launch_bounds__(kThreads, 5) row_fwd_kernel(FwdParams p, int t
           const float alpha = (m == -INFINITY) ? 0.f : exp_clamped(m - m_new);
           float w = ok ? exp_clamped(sc - m_new) : 0.f;
           l = l * alpha + warp_sum(w);
-          if (p.v_scale_mode == 2 && ok) {
-            const int key = k0 + jl;
-            const int page = key / p.block_size;
-            const long long id = page_block_id(p, sl.bh, page);
-            w *= __ldg(p.v_scale + id * p.block_size + (key - page * p.block_size));
-          }
-          w *= kTwoPow120;
 #pragma unroll
           for (int i = 0; i < DPL; ++i) acc[i] *= alpha;
           const uint8_t* vbase = &sm.v[s][(cw * kKeysPerWarp) * D];
-#pragma unroll 4
-          for (int jj = 0; jj < kKeysPerWarp; ++jj) {
-            const float wj = __shfl_sync(0xffffffffu, w, jj);
-            if (wj != 0.f) {
-              uint32_t vw[(DPL + 3) / 4];
+          if (p.v_scale_mode != 2) {
+            // Products on f16x2: w in [0, 1] and the decode / 256 in [-1.75, 1.75], so
+            // the sums over this warp's 16 keys stay below 28; they are added to the
+            // f32 accumulators once per stage.  A key that is absent has w = 0, and
+            // whatever bytes its V row holds decode to finite f16 values (the
+            // exponent field never reaches 31), so its products are 0.
+            const uint32_t w2 = pack_f16x2(w, w);
+            uint32_t pe[NW], po[NW];
+#pragma unroll
+            for (int i = 0; i < NW; ++i) pe[i] = po[i] = 0u;
+#pragma unroll
+            for (int jj = 0; jj < kKeysPerWarp; ++jj) {
+              const uint32_t wj = __shfl_sync(0xffffffffu, w2, jj);
+              uint32_t vw[NW];
               load_v_lane<D>(vbase + jj * D, lane, vw);
 #pragma unroll
-              for (int i = 0; i < DPL; ++i) {
-                acc[i] = fmaf(wj, fp8_bits_to_f32_scaled(vw[i >> 2] >> (8 * (i & 3))), acc[i]);
+              for (int i = 0; i < NW; ++i) {
+                pe[i] = hfma2(wj, fp8x2_even_to_f16x2_div256(vw[i]), pe[i]);
+                po[i] = hfma2(wj, fp8x2_odd_to_f16x2_div256(vw[i]), po[i]);
+              }
+            }
+            // pe[i] holds dims 4i and 4i+2 of this lane, po[i] dims 4i+1 and 4i+3.
+#pragma unroll
+            for (int i = 0; i < NW; ++i) {
+              acc[4 * i + 0] = fmaf(f16_lo_to_f32(pe[i]), 256.f, acc[4 * i + 0]);
+              acc[4 * i + 1] = fmaf(f16_lo_to_f32(po[i]), 256.f, acc[4 * i + 1]);
+              acc[4 * i + 2] = fmaf(f16_hi_to_f32(pe[i]), 256.f, acc[4 * i + 2]);
+              acc[4 * i + 3] = fmaf(f16_hi_to_f32(po[i]), 256.f, acc[4 * i + 3]);
+            }
+          } else {
+            // Per-slot V scale: w times the key's own scale, products in f32.
+            if (ok) {
+              const int key = k0 + jl;
+              const int page = key / p.block_size;
+              const long long id = page_block_id(p, sl.bh, page);
+              w *= __ldg(p.v_scale + id * p.block_size + (key - page * p.block_size));
+            }
+            w *= kTwoPow120;
+#pragma unroll 4
+            for (int jj = 0; jj < kKeysPerWarp; ++jj) {
+              const float wj = __shfl_sync(0xffffffffu, w, jj);
+              if (wj != 0.f) {
+                uint32_t vw[NW];
+                load_v_lane<D>(vbase + jj * D, lane, vw);
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) {
+                  acc[i] = fmaf(wj, fp8_bits_to_f32_scaled(vw[i >> 2] >> (8 * (i & 3))), acc[i]);
+                }
               }
             }
           }

@@ -134,12 +134,6 @@ __device__ __forceinline__ uint32_t sw128_off(uint32_t r, uint32_t c) {
   return (r >> 3) * 1024u + (r & 7u) * 128u + ((c ^ (r & 7u)) << 4);
 }
 
-__device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
-  uint32_t r;
-  asm("cvt.rn.f16x2.f32 %0, %2, %1;" : "=r"(r) : "f"(a), "f"(b));
-  return r;
-}
-
 // Stores 16 consecutive output values of one row (f32, bf16 or f16).
 template <int kDtype>
 __device__ __forceinline__ void store_row16(void* o, long long base, const float (&v)[16]) {
