@@ -20,13 +20,19 @@
 //     finalised (:582-593) or written as a split-KV partial for the combine kernel.
 #pragma once
 
+#include <climits>
+
 #include "common.cuh"
 
 namespace hyp {
 namespace row {
 
 constexpr int kKeysPerStage = 64;
-constexpr int kStages = 4;
+// Two 64-key stages per CTA and 8 CTAs per SM: on B200 more resident CTAs with a
+// shallow ring hide the HBM latency better than fewer CTAs with a deep one
+// (decode B64 H32 S_kv 8192: 2 x 8 reaches 84 % of the measured copy bandwidth,
+// 4 x 5 reaches 76 %).
+constexpr int kStages = 2;
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = 32 * (1 + kConsumerWarps);
 constexpr int kKeysPerWarp = kKeysPerStage / kConsumerWarps;  // 16
@@ -60,6 +66,7 @@ struct Smem {
   float merge_m[kConsumerWarps];
   float merge_l[kConsumerWarps];
   float merge_acc[kConsumerWarps][D];
+  alignas(16) uint32_t wbuf[kConsumerWarps][kKeysPerWarp];  // f16x2 {w, w} of each warp's keys
   alignas(8) uint64_t full[kStages];
   alignas(8) uint64_t empty[kStages];
   alignas(8) uint64_t unit_full[2];
@@ -67,11 +74,6 @@ struct Smem {
   int abort;
 };
 
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -93,7 +95,7 @@ __device__ __forceinline__ void load_v_lane(const uint8_t* row, int lane, uint32
 }
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 5) row_fwd_kernel(FwdParams p, int total_units) {
+__global__ void __launch_bounds__(kThreads, 8) row_fwd_kernel(FwdParams p, int total_units) {
   constexpr int W = D / 32;
   constexpr int DPL = D / 32;  // dims per lane
   constexpr int NW = DPL / 4;  // 32-bit words of V bytes per lane and key
@@ -266,19 +268,31 @@ __global__ void __launch_bounds__(kThreads, 5) row_fwd_kernel(FwdParams p, int t
         const unsigned long long mask = sm.hdr[s].mask;
         const int jl = cw * kKeysPerWarp + (lane & 15);
         const bool ok = (lane < 16) && (jl < n) && ((mask >> jl) & 1ull);
-        float sc = -INFINITY;
+        int si = 0;
         if (ok) {
           const uint32_t* kr = reinterpret_cast<const uint32_t*>(&sm.k[s][jl * W * 4]);
-          const int si = sign_score<W>(q, kr);
-          sc = (float)si * p.inv_sqrt_d;
+          si = sign_score<W>(q, kr);
           if (p.debug_scores) p.debug_scores[(long long)sl.item * p.debug_ld + (k0 + jl)] = si;
         }
-        const float mt = warp_max(sc);
-        if (mt != -INFINITY) {
+        // The largest score of the group is the extreme integer score times
+        // inv_sqrt_d (the product is monotonic): one warp reduction on integers.
+        // Scores lie in [-D, D], so the sentinels mark a group with no key.
+        int ext;
+        bool any;
+        if (p.inv_sqrt_d >= 0.f) {
+          ext = __reduce_max_sync(0xffffffffu, ok ? si : INT_MIN);
+          any = ext != INT_MIN;
+        } else {
+          ext = __reduce_min_sync(0xffffffffu, ok ? si : INT_MAX);
+          any = ext != INT_MAX;
+        }
+        if (any) {
+          const float mt = (float)ext * p.inv_sqrt_d;
+          const float sc = (float)si * p.inv_sqrt_d;
           const float m_new = fmaxf(m, mt);
           const float alpha = (m == -INFINITY) ? 0.f : exp_clamped(m - m_new);
           float w = ok ? exp_clamped(sc - m_new) : 0.f;
-          l = l * alpha + warp_sum(w);
+          l = l * alpha + w;  // per lane; summed over the warp once per unit
 #pragma unroll
           for (int i = 0; i < DPL; ++i) acc[i] *= alpha;
           const uint8_t* vbase = &sm.v[s][(cw * kKeysPerWarp) * D];
@@ -288,19 +302,24 @@ __global__ void __launch_bounds__(kThreads, 5) row_fwd_kernel(FwdParams p, int t
             // f32 accumulators once per stage.  A key that is absent has w = 0, and
             // whatever bytes its V row holds decode to finite f16 values (the
             // exponent field never reaches 31), so its products are 0.
-            const uint32_t w2 = pack_f16x2(w, w);
+            if (lane < kKeysPerWarp) sm.wbuf[cw][lane] = pack_f16x2(w, w);
+            __syncwarp();
             uint32_t pe[NW], po[NW];
 #pragma unroll
             for (int i = 0; i < NW; ++i) pe[i] = po[i] = 0u;
 #pragma unroll
-            for (int jj = 0; jj < kKeysPerWarp; ++jj) {
-              const uint32_t wj = __shfl_sync(0xffffffffu, w2, jj);
-              uint32_t vw[NW];
-              load_v_lane<D>(vbase + jj * D, lane, vw);
+            for (int j4 = 0; j4 < kKeysPerWarp; j4 += 4) {
+              const uint4 w4 = *reinterpret_cast<const uint4*>(&sm.wbuf[cw][j4]);
+              const uint32_t wq[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-              for (int i = 0; i < NW; ++i) {
-                pe[i] = hfma2(wj, fp8x2_even_to_f16x2_div256(vw[i]), pe[i]);
-                po[i] = hfma2(wj, fp8x2_odd_to_f16x2_div256(vw[i]), po[i]);
+              for (int u = 0; u < 4; ++u) {
+                uint32_t vw[NW];
+                load_v_lane<D>(vbase + (j4 + u) * D, lane, vw);
+#pragma unroll
+                for (int i = 0; i < NW; ++i) {
+                  pe[i] = hfma2(wq[u], fp8x2_even_to_f16x2_div256(vw[i]), pe[i]);
+                  po[i] = hfma2(wq[u], fp8x2_odd_to_f16x2_div256(vw[i]), po[i]);
+                }
               }
             }
             // pe[i] holds dims 4i and 4i+2 of this lane, po[i] dims 4i+1 and 4i+3.
@@ -344,9 +363,10 @@ __global__ void __launch_bounds__(kThreads, 5) row_fwd_kernel(FwdParams p, int t
       const bool stop = aborted || (*abort != 0);
 
       // ---- merge the four warps' (m, l, acc) ----
+      const float l_warp = warp_sum(l);
       if (lane == 0) {
         sm.merge_m[cw] = m;
-        sm.merge_l[cw] = l;
+        sm.merge_l[cw] = l_warp;
       }
 #pragma unroll
       for (int i = 0; i < DPL; ++i) sm.merge_acc[cw][lane * DPL + i] = acc[i];
