@@ -87,15 +87,16 @@ int get_dev(const DevInfo** out) {
   return HYPERION_OK;
 }
 
-// KV splits per item of the row kernel.  Enough units that every CTA slot gets
-// about 16 of them (balance), no split below 512 keys, none above 8192 keys when
-// the table allows longer contexts, and at most 16.
+// KV splits per item of the row kernel.  A worklist that alone gives every CTA
+// slot about 16 units is not split.  A shorter one is split until it does, and
+// at least into pieces of at most 8192 keys of the table; no piece is shorter
+// than 512 keys, and an item has at most 16 pieces.
 int choose_splits(const DevInfo& di, int D, int total_work, long long max_keys) {
   if (total_work <= 0) return 1;
   const int ctas = (D == 256) ? di.row_ctas_256 : di.row_ctas_128;
   const long long target = (long long)di.n_sm * ctas * 16;
-  long long ns = 1;
-  if (total_work < target) ns = (target + total_work - 1) / total_work;
+  if (total_work >= target) return 1;
+  long long ns = (target + total_work - 1) / total_work;
   ns = std::max<long long>(ns, (max_keys + 8191) / 8192);
   ns = std::min<long long>(ns, std::max<long long>(1, max_keys / 512));
   ns = std::min<long long>(ns, 16);
@@ -107,17 +108,12 @@ size_t partial_bytes(int total_work, int n_split, int D) {
   return (size_t)total_work * n_split * (2 + D) * sizeof(float);
 }
 
+// Workspace of the automatic split choice (a forced num_splits needs
+// 256 + total_work * num_splits * (2 + head_dim) * 4 bytes).
 size_t workspace_needed(const DevInfo& di, int total_work, int D, int block_size, int num_blocks) {
   const long long max_keys = (long long)std::max(block_size, 1) * std::max(num_blocks, 1);
-  // Worst case over the automatic choice and any forced num_splits (capped at 16).
-  const int ns = std::max(choose_splits(di, D, total_work, max_keys), 16);
-  return hyp::kWsPartials + partial_bytes(total_work, ns, D);
+  return hyp::kWsPartials + partial_bytes(total_work, choose_splits(di, D, total_work, max_keys), D);
 }
-
-struct Call {
-  hyp::FwdParams p;
-  int total_work;
-};
 
 }  // namespace
 

@@ -172,6 +172,8 @@ def hyperion_apex_kernel(
     with torch.cuda.device(dev):
         need = _capi.lib.hyperion_workspace_bytes(total_work, head_dim, block_size, num_blocks)
         _check(need > 0, f"hyperion_workspace_bytes failed: {_capi.last_error()}")
+        if num_splits > 1:  # a forced split count: its partials, (m, l, acc[head_dim]) f32 per unit
+            need = max(need, 256 + total_work * min(int(num_splits), 16) * (2 + head_dim) * 4)
         ws = _workspace(dev, need)
         stream = torch.cuda.current_stream(dev).cuda_stream
         rc = _capi.lib.hyperion_apex_kernel_ex(

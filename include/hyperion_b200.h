@@ -100,7 +100,9 @@ typedef struct hyperion_options {
   int64_t debug_ld;      /* row stride of debug_scores in elements */
 } hyperion_options;
 
-/* Bytes of device workspace the forward needs for these sizes (an upper bound). */
+/* Bytes of device workspace the forward needs for these sizes with the automatic
+ * KV-split choice.  A call that forces hyperion_options.num_splits = n > 1 needs
+ * 256 + total_work * n * (2 + head_dim) * 4 bytes. */
 size_t hyperion_workspace_bytes(int32_t total_work, int32_t head_dim,
                                 int32_t block_size, int32_t num_blocks);
 
