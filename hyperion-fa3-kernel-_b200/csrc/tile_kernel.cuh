@@ -7,26 +7,29 @@
 // causal rows first.  The unit's keys are walked in 128-key tiles:
 //
 //   loader warp    cp.async.bulk of the raw page pieces (sign bits 16 B/key, FP8
-//                  codes 128 B/key) into a 3-stage ring, with the key-valid mask
+//                  codes 128 B/key) into a 2-stage ring, with the key-valid mask
 //                  (context length, page ids inside the pool; :402-411, :479-486);
 //   converters     (4 warps) sign bits -> e4m3 +-1 bytes in the 128B-swizzled
 //                  K-major layout; FP8 codes -> f16 (the reference's decode,
 //                  :122-141, divided by 256, exact) in the 128B-swizzled MN-major
 //                  layout; Q rows of the unit likewise, once per unit;
-//   MMA warp       S_t = Q_t K^T as a kind::f8f6f4 tcgen05.mma (the +-1 products
-//                  sum to D - 2*popcount(q XOR k) exactly in the f32 accumulator,
-//                  README.md:22), then O_t += P_t V, a kind::f16 MMA with P read
-//                  from TMEM; tcgen05.commit hands each result on;
+//   MMA warps      (one per Q tile) S_t = Q_t K^T as kind::f8f6f4 tcgen05.mmas
+//                  (the +-1 products sum to D - 2*popcount(q XOR k) exactly in the
+//                  f32 accumulator, README.md:22), then O_t += P_t V, kind::f16
+//                  MMAs with P read from TMEM; tcgen05.commit hands each result on;
 //   softmax WG t   (4 warps per Q tile, one thread per row = TMEM lane) reads S,
 //                  applies the masks (causal: key > q_idx, :483-486), keeps the
 //                  running max with the reference's online update (:544-572),
 //                  writes P as f16 over S, and at the end of the unit finalises
-//                  O = acc * (l > 1e-6 ? 1/l : 1) (:582-593).  The two warpgroups
-//                  take turns for their exponential passes (ping-pong), so one
-//                  runs while the tensor core serves the other's MMAs.
+//                  O = acc * (l > 1e-6 ? 1/l : 1) (:582-593).
 //
-// TMEM (512 columns): Q tile t owns S/P at [256t, 256t+128) and O at
-// [256t+128, 256t+256).  Every mbarrier wait is bounded; on a timeout the CTA
+// Each 128-key tile is handled in two 64-key halves.  TMEM (512 columns): Q tile t
+// owns S at [256t, 256t+128) -- half A (keys 0-63) in the first 64 columns, half B
+// in the next 64 -- and O at [256t+128, 256t+256); P of a half is written over the
+// first 32 columns of that half's S.  The QK of half A of tile g+1 only has to wait
+// for the PV of half A of tile g, so it runs on the tensor core while the softmax
+// is still on half B of tile g: the next scores are ready when the softmax wants
+// them, and the two Q tiles' softmax passes overlap each other.  Every mbarrier wait is bounded; on a timeout the CTA
 // raises HYPERION_DEVERR_WAIT_TIMEOUT, lets in-flight copies and MMAs land,
 // frees TMEM and exits.
 #pragma once
@@ -41,14 +44,14 @@ constexpr int kRows = 128;
 constexpr int kQTiles = 2;
 constexpr int kChunk = kRows * kQTiles;
 constexpr int kKeys = 128;  // keys per KV tile
-constexpr int kRawStages = 3;
-constexpr int kKvStages = 2;
-constexpr int kMmaWarp = 8;
-constexpr int kLoadWarp = 9;
-constexpr int kConvWarp0 = 10;
+constexpr int kRawStages = 2;
+constexpr int kKvStages = 3;
+constexpr int kMmaWarp = 8;  // warps 8 and 9: the MMA issuers of Q tiles 0 and 1
+constexpr int kLoadWarp = 10;
+constexpr int kConvWarp0 = 11;
 constexpr int kConvWarps = 4;
-constexpr int kThreads = 32 * (kConvWarp0 + kConvWarps);  // 448
-constexpr int kSchedConsumers = 4 * kQTiles + 1 + kConvWarps;  // warps that read each unit
+constexpr int kThreads = 32 * (kConvWarp0 + kConvWarps);  // 480
+constexpr int kSchedConsumers = 4 * kQTiles + kQTiles + kConvWarps;  // warps that read each unit
 constexpr uint32_t kTmemCols = 512;
 constexpr int kKTileBytes = kKeys * 128;      // e4m3 +-1, K-major SW128
 constexpr int kVTileBytes = kKeys * 256;      // f16, MN-major SW128: two 64-dim blocks
@@ -56,6 +59,12 @@ constexpr int kVBlockBytes = kKeys * 128;     // one 64-dim block (LBO of the V 
 // Lazy rescale threshold: P = exp(s - m) may grow to 2^8 before the running max
 // is moved (8 / log2(e) in score units), well inside the f16 range of P.
 constexpr float kTauS = 5.545177444479562f;
+// Integer scores of head_dim 128 lie in [-128, 128] and all have the parity of 128, so
+// a score minus the row's integer maximum is 2(j - 128) for a j in [0, 256].
+constexpr int kPTabRows = 257;
+// Odd columns' weights by table lookup instead of the exponential unit (the table
+// takes 33 KB of shared memory, which then has no room for a third KV stage).
+constexpr bool kPTable = false;
 
 struct UnitInfo {
   int kind;     // 0 stop, 1 work
@@ -77,6 +86,10 @@ struct Smem {
   alignas(128) uint8_t raw_k[kRawStages][kKeys * 16];
   alignas(128) uint8_t raw_v[kRawStages][kKeys * 128];
   uint32_t raw_mask[kRawStages][4];
+  // Softmax weights by table: entry j (one copy per lane, so a warp's lookups never
+  // share a bank) holds exp(max(|c| * 2(j - 128), -80)), the weight of a score that
+  // lies 2(j - 128) above the row's running integer maximum (|c| = |inv_sqrt_d|).
+  alignas(128) float ptab[kPTable ? kPTabRows : 1][32];
   uint32_t kv_mask[kKvStages][4];
   UnitInfo unit[2];
   alignas(8) uint64_t sched_full[2];
@@ -87,12 +100,11 @@ struct Smem {
   alignas(8) uint64_t kv_empty[kKvStages];
   alignas(8) uint64_t q_full;
   alignas(8) uint64_t q_empty;
-  alignas(8) uint64_t s_full[kQTiles];
-  alignas(8) uint64_t p_full[kQTiles];
+  alignas(8) uint64_t s_full[kQTiles][2];  // [tile][half]: S of that half of the next KV tile
+  alignas(8) uint64_t p_full[kQTiles][2];  // [tile][half]: P of that half written
   alignas(8) uint64_t o_full[kQTiles];
   alignas(8) uint64_t o_empty[kQTiles];
-  alignas(8) uint64_t turn[kQTiles];  // softmax ping-pong: warpgroup t may run its P pass
-  alignas(8) uint64_t drain;
+  alignas(8) uint64_t drain[kQTiles];
   uint32_t tmem_base;
   int abort;
 };
@@ -239,10 +251,37 @@ __device__ __forceinline__ float row_tile_max(uint32_t s_col, const uint32_t (&m
   return fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
 }
 
-// Exponentials 2^(v*k2 + bias) of one 16-column chunk.
-__device__ __forceinline__ void p_exp16(const uint32_t (&v)[16], float k2, float bias, float (&e)[16]) {
+// The weight exp(|c| (S - S_m)) of an integer score S (exact in f32) relative to the
+// row's integer maximum S_m, computed two ways that agree to rounding: on the
+// exponential unit as 2^(S*k2 + bias) with bias = -S_m*k2, or by a lookup in the
+// table.  Alternating them keeps the exponential unit and the load/ALU pipes busy
+// together.  For the lookup, fmaf(S, 64, c) with c = 2^23 + 16384 - 64*S_m + 4*lane
+// is 2^23 plus the entry's byte offset (64 (S - S_m) + 16384 = 128 j, plus 4*lane for
+// this lane's copy), exact for every pair of scores, so the float's bits minus those
+// of 2^23 give the offset.
+struct PExp {
+  float k2, bias;  // exponential unit
+  float c;         // table: 2^23 + 16384 - 64*S_m + 4*lane
+  uint32_t a;      // table: shared address of entry 0 minus the bits of 2^23
+};
+
+__device__ __forceinline__ float pexp_mufu(uint32_t s, const PExp& x) {
+  return ex2_approx(fmaf(__uint_as_float(s), x.k2, x.bias));
+}
+__device__ __forceinline__ float pexp_lut(uint32_t s, const PExp& x) {
+  const uint32_t addr = __float_as_uint(fmaf(__uint_as_float(s), 64.f, x.c)) + x.a;
+  float r;
+  asm("ld.shared.f32 %0, [%1];" : "=f"(r) : "r"(addr));
+  return r;
+}
+
+// Weights of one 16-column chunk: even columns on the exponential unit, odd ones by table.
+__device__ __forceinline__ void p_exp16(const uint32_t (&v)[16], const PExp& x, float (&e)[16]) {
 #pragma unroll
-  for (int i = 0; i < 16; ++i) e[i] = ex2_approx(fmaf(__uint_as_float(v[i]), k2, bias));
+  for (int i = 0; i < 16; i += 2) {
+    e[i] = pexp_mufu(v[i], x);
+    e[i + 1] = kPTable ? pexp_lut(v[i + 1], x) : pexp_mufu(v[i + 1], x);
+  }
 }
 
 // Finishes chunk h (exponentials in `e`: mask, add to l[], pack to f16 pairs, store
@@ -251,13 +290,13 @@ __device__ __forceinline__ void p_exp16(const uint32_t (&v)[16], float k2, float
 // 8 cycles, and the finishing work of chunk h fills the issue slots in between.
 template <bool kMasked, bool kNext>
 __device__ __forceinline__ void p_step(uint32_t s_col, int h, float (&e)[16], uint32_t bits, const uint32_t (&vn)[16],
-                                       float (&en)[16], float k2, float bias, float (&l)[4]) {
+                                       float (&en)[16], const PExp& x, float (&l)[4]) {
   uint32_t pk[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     if (kNext) {
-      en[2 * i] = ex2_approx(fmaf(__uint_as_float(vn[2 * i]), k2, bias));
-      en[2 * i + 1] = ex2_approx(fmaf(__uint_as_float(vn[2 * i + 1]), k2, bias));
+      en[2 * i] = pexp_mufu(vn[2 * i], x);
+      en[2 * i + 1] = kPTable ? pexp_lut(vn[2 * i + 1], x) : pexp_mufu(vn[2 * i + 1], x);
     }
     float e0 = e[2 * i], e1 = e[2 * i + 1];
     if (kMasked) {
@@ -270,12 +309,13 @@ __device__ __forceinline__ void p_step(uint32_t s_col, int h, float (&e)[16], ui
   tc::st8(s_col + 8 * h, pk);
 }
 
-// P = 2^(S*k2 + bias) for this thread's row over the 128-key tile; returns sum(P).
-// While chunk h is finished, the exponentials of chunk h+1 run and the TMEM load of
-// chunk h+2 is in flight.
+// P = exp(|c| (S - S_m)) for this thread's row over one 64-key half of the tile (S
+// at s_col, 16-key chunks c0 .. c0+3 of the tile); returns sum(P).  While chunk h is
+// finished, the exponentials of chunk h+1 run and the TMEM load of chunk h+2 is in
+// flight.  P of chunk h goes to columns [8h, 8h+8) of the half, over S already read.
 template <bool kMasked>
-__device__ __forceinline__ float row_tile_p(uint32_t s_col, const uint32_t (&mk)[4], int kbase, int row_end, float k2,
-                                           float bias) {
+__device__ __forceinline__ float row_half_p(uint32_t s_col, const uint32_t (&mk)[4], int c0, int kbase, int row_end,
+                                           const PExp& x) {
   float l[4] = {0.f, 0.f, 0.f, 0.f};
   uint32_t va[16], vb[16];
   float ea[16], eb[16];
@@ -283,20 +323,15 @@ __device__ __forceinline__ float row_tile_p(uint32_t s_col, const uint32_t (&mk)
   tc::ld16(s_col + 16, vb);
   tc::ld_wait_regs(va);
   tc::ld_wait_regs(vb);
-  p_exp16(va, k2, bias, ea);
-#pragma unroll 1
-  for (int h = 0; h < 6; h += 2) {
-    // va is free (chunk h's exponentials are in ea): load chunk h+2 into it.
-    tc::ld16(s_col + 16 * (h + 2), va);
-    p_step<kMasked, true>(s_col, h, ea, kMasked ? chunk_bits(mk, h, kbase, row_end) : 0xFFFFu, vb, eb, k2, bias, l);
-    tc::ld_wait_regs(va);
-    tc::ld16(s_col + 16 * (h + 3), vb);
-    p_step<kMasked, true>(s_col, h + 1, eb, kMasked ? chunk_bits(mk, h + 1, kbase, row_end) : 0xFFFFu, va, ea, k2, bias,
-                          l);
-    tc::ld_wait_regs(vb);
-  }
-  p_step<kMasked, true>(s_col, 6, ea, kMasked ? chunk_bits(mk, 6, kbase, row_end) : 0xFFFFu, vb, eb, k2, bias, l);
-  p_step<kMasked, false>(s_col, 7, eb, kMasked ? chunk_bits(mk, 7, kbase, row_end) : 0xFFFFu, va, ea, k2, bias, l);
+  p_exp16(va, x, ea);
+  tc::ld16(s_col + 32, va);
+  p_step<kMasked, true>(s_col, 0, ea, kMasked ? chunk_bits(mk, c0, kbase, row_end) : 0xFFFFu, vb, eb, x, l);
+  tc::ld_wait_regs(va);
+  tc::ld16(s_col + 48, vb);
+  p_step<kMasked, true>(s_col, 1, eb, kMasked ? chunk_bits(mk, c0 + 1, kbase, row_end) : 0xFFFFu, va, ea, x, l);
+  tc::ld_wait_regs(vb);
+  p_step<kMasked, true>(s_col, 2, ea, kMasked ? chunk_bits(mk, c0 + 2, kbase, row_end) : 0xFFFFu, vb, eb, x, l);
+  p_step<kMasked, false>(s_col, 3, eb, kMasked ? chunk_bits(mk, c0 + 3, kbase, row_end) : 0xFFFFu, va, ea, x, l);
   return (l[0] + l[1]) + (l[2] + l[3]);
 }
 
@@ -354,24 +389,30 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     }
     for (int i = 0; i < kKvStages; ++i) {
       mbar_init(&sm.kv_full[i], kConvWarps);
-      mbar_init(&sm.kv_empty[i], 1);
+      mbar_init(&sm.kv_empty[i], kQTiles);  // a commit from each MMA issuer
     }
     mbar_init(&sm.q_full, kConvWarps);
-    mbar_init(&sm.q_empty, 1);
+    mbar_init(&sm.q_empty, kQTiles);
     for (int t = 0; t < kQTiles; ++t) {
-      mbar_init(&sm.s_full[t], 1);
-      mbar_init(&sm.p_full[t], 4);
+      for (int h = 0; h < 2; ++h) {
+        mbar_init(&sm.s_full[t][h], 1);
+        mbar_init(&sm.p_full[t][h], 4);
+      }
       mbar_init(&sm.o_full[t], 1);
       mbar_init(&sm.o_empty[t], 4);
-      mbar_init(&sm.turn[t], 4);
+      mbar_init(&sm.drain[t], 1);
     }
-    mbar_init(&sm.drain, 1);
     sm.abort = 0;
     fence_mbar_init();
   }
   if (warp == kMmaWarp) {
     tc::tmem_alloc(&sm.tmem_base, kTmemCols);
     tc::tmem_relinquish();
+  }
+  if (kPTable) {
+    const float cabs = fabsf(p.inv_sqrt_d);
+    for (int i = threadIdx.x; i < kPTabRows * 32; i += kThreads)
+      sm.ptab[i >> 5][i & 31] = expf(fmaxf(cabs * (float)(2 * ((i >> 5) - 128)), kExpClamp));
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -634,37 +675,38 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       }
       if (ab) break;
     }
-  } else if (warp == kMmaWarp) {
-    // ================================================================ MMA issuer
-    // One thread issues every MMA and commit (a tcgen05.commit tracks the MMAs of
-    // the thread that issues it); QK with N = 128 and PV with N = 128 keep each
-    // instruction at the tensor core's full per-instruction rate.
+  } else if (warp >= kMmaWarp && warp < kMmaWarp + kQTiles) {
+    // ================================================================ MMA issuers
+    // Warp kMmaWarp + t issues every MMA and commit of Q tile t from one thread (a
+    // tcgen05.commit tracks the MMAs of the thread that issues it, and the MMAs of
+    // one thread run in order).  Per KV tile g and half h: PV(g, h) as soon as the
+    // softmax has written P of that half, then QK(g+1, h) into the same S columns.
+    const int t = warp - kMmaWarp;
     if (lane == 0) {
       uint32_t uc = 0, kvit = 0, uq = 0, uo = 0;
-      uint32_t pc[kQTiles] = {0u, 0u};
       const uint32_t q_base = smem_u32(&sm.q[0][0]);
       const uint32_t k_base = smem_u32(&sm.kt[0][0]);
       const uint32_t v_base = smem_u32(&sm.vt[0][0]);
       const uint64_t q_desc = tc::sw128_desc(q_base, 16, 1024);
       const uint64_t k_desc = tc::sw128_desc(k_base, 16, 1024);
       const uint64_t v_desc = tc::sw128_desc(v_base, kVBlockBytes, 1024);
+      const uint32_t s_tm = tmem + (uint32_t)(t * 256);
+      const uint32_t o_tm = s_tm + 128;
+      const uint64_t ad = q_desc + (uint64_t)(t * (kRows * 128) / 16);
       bool ab = false;
-      // S_t = Q_t K(stage s)^T  (M 128, N 128, K 128 in 4 steps of 32 bytes)
-      auto qk = [&](int t, int s) {
-        const uint32_t d = tmem + (uint32_t)(t * 256);
-        const uint64_t ad = q_desc + (uint64_t)(t * (kRows * 128) / 16);
-        const uint64_t bd = k_desc + (uint64_t)(s * kKTileBytes / 16);
+      // S half h = Q_t K(stage s, keys 64h .. 64h+63)^T  (M 128, N 64, K 128 in 4 steps)
+      auto qk = [&](int s, int h) {
+        const uint64_t bd = k_desc + (uint64_t)((s * kKTileBytes + h * 64 * 128) / 16);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) tc::mma_f8f6f4_ss(d, ad + 2 * kk, bd + 2 * kk, tc::kIdescQK, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk)
+          tc::mma_f8f6f4_ss(s_tm + 64u * h, ad + 2 * kk, bd + 2 * kk, tc::kIdescQK64, kk > 0 ? 1u : 0u);
       };
-      // O_t (+)= P_t V(stage s)  (M 128, N 128, K 128 keys in 8 steps of 16)
-      auto pv = [&](int t, int s, bool acc) {
-        const uint32_t d = tmem + (uint32_t)(t * 256 + 128);
-        const uint32_t a = tmem + (uint32_t)(t * 256);
-        const uint64_t bd = v_desc + (uint64_t)(s * kVTileBytes / 16);
+      // O_t (+)= P(half h) V(stage s, keys 64h .. 64h+63)  (M 128, N 128, K 64 keys in 4 steps)
+      auto pv = [&](int s, int h, bool acc) {
+        const uint64_t bd = v_desc + (uint64_t)(s * kVTileBytes / 16) + 128u * 4u * h;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          tc::mma_f16_ts(d, a + kk * 8, bd + 128 * kk, tc::kIdescPV, (acc || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk)
+          tc::mma_f16_ts(o_tm, s_tm + 64u * h + 8u * kk, bd + 128 * kk, tc::kIdescPV, (acc || kk > 0) ? 1u : 0u);
       };
       for (;;) {
         if (!mbar_wait(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) break;
@@ -679,40 +721,46 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         int s = kvit % kKvStages;
         if (!mbar_wait(&sm.kv_full[s], (kvit / kKvStages) & 1, abort, p.err)) break;
         tc::fence_after_sync();
-        for (int t = 0; t < kQTiles; ++t) {
-          qk(t, s);
-          tc::commit(&sm.s_full[t]);
-        }
+        qk(s, 0);
+        tc::commit(&sm.s_full[t][0]);
+        qk(s, 1);
+        tc::commit(&sm.s_full[t][1]);
         if (n == 1) tc::commit(&sm.q_empty);
-        for (int j = 0; j < n && !ab; ++j) {
-          s = (kvit + j) % kKvStages;
-          const uint32_t nxt = kvit + j + 1;
-          for (int t = 0; t < kQTiles; ++t) {
-            if (!mbar_wait(&sm.p_full[t], pc[t] & 1, abort, p.err) ||
-                (j == 0 && !mbar_wait(&sm.o_empty[t], (uo & 1) ^ 1, abort, p.err))) {
+        for (int j = 0; j < n; ++j) {
+          const uint32_t g = kvit + j;
+          s = g % kKvStages;
+          const uint32_t nxt = g + 1;
+          const int s2 = nxt % kKvStages;
+          // ---- half A
+          if (!mbar_wait(&sm.p_full[t][0], g & 1, abort, p.err) ||
+              (j == 0 && !mbar_wait(&sm.o_empty[t], (uo & 1) ^ 1, abort, p.err))) {
+            ab = true;
+            break;
+          }
+          tc::fence_after_sync();
+          pv(s, 0, j > 0);
+          if (j + 1 < n) {
+            if (!mbar_wait(&sm.kv_full[s2], (nxt / kKvStages) & 1, abort, p.err)) {
               ab = true;
               break;
             }
-            ++pc[t];
             tc::fence_after_sync();
-            pv(t, s, j > 0);
-            if (j == n - 1) tc::commit(&sm.o_full[t]);
-            if (t == kQTiles - 1) tc::commit(&sm.kv_empty[s]);
-            // The QK of the next tile reuses this Q tile's S/P columns: it is issued
-            // after the PV that reads P (tcgen05 MMAs of one thread run in order).
-            if (j + 1 < n) {
-              const int s2 = nxt % kKvStages;
-              if (t == 0) {
-                if (!mbar_wait(&sm.kv_full[s2], (nxt / kKvStages) & 1, abort, p.err)) {
-                  ab = true;
-                  break;
-                }
-                tc::fence_after_sync();
-              }
-              qk(t, s2);
-              tc::commit(&sm.s_full[t]);
-              if (t == kQTiles - 1 && j + 2 == n) tc::commit(&sm.q_empty);
-            }
+            qk(s2, 0);
+            tc::commit(&sm.s_full[t][0]);
+          }
+          // ---- half B
+          if (!mbar_wait(&sm.p_full[t][1], g & 1, abort, p.err)) {
+            ab = true;
+            break;
+          }
+          tc::fence_after_sync();
+          pv(s, 1, true);
+          if (j == n - 1) tc::commit(&sm.o_full[t]);
+          tc::commit(&sm.kv_empty[s]);
+          if (j + 1 < n) {
+            qk(s2, 1);
+            tc::commit(&sm.s_full[t][1]);
+            if (j + 2 == n) tc::commit(&sm.q_empty);
           }
         }
         if (ab) break;
@@ -720,8 +768,8 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         ++uo;
       }
       // Every MMA issued must land before TMEM is released.
-      tc::commit(&sm.drain);
-      mbar_drain(&sm.drain, 0);
+      tc::commit(&sm.drain[t]);
+      mbar_drain(&sm.drain[t], 0);
     }
     __syncwarp();
   } else {
@@ -739,7 +787,8 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     // Running max from which on a row needs no max pass: (head_dim * |inv_sqrt_d|)
     // minus 11, so exp(s - m) <= e^11 < 2^15.9 for every possible score s.
     const float m_safe = 128.f * cabs - 11.0f;
-    uint32_t uc = 0, kvit = 0, sc = 0, oc = 0;
+    const uint32_t tab_addr = smem_u32(&sm.ptab[0][0]);
+    uint32_t uc = 0, kvit = 0, oc = 0;
     for (;;) {
       if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) break;
       int n_tiles, bh, row_end, item;
@@ -773,15 +822,15 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         continue;
       }
       float m = -INFINITY, l = 0.f;
+      int s_m = 0;  // integer score whose scaled value is m (0 while m = -inf)
       bool ab = false;
       for (int j = 0; j < n_tiles; ++j) {
         const uint32_t g = kvit;
         const int s = g % kKvStages;
-        if (!mbar_wait_warp(&sm.s_full[t], sc & 1, abort, p.err)) {
+        if (!mbar_wait_warp(&sm.s_full[t][0], g & 1, abort, p.err)) {
           ab = true;
           break;
         }
-        ++sc;
         uint32_t mk[4] = {0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu};
         if (!p.pages_all_valid) {
           // Page ids can fall outside the pool: read the tile's key mask (the
@@ -795,43 +844,66 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         }
         tc::fence_after_sync();
         const int k0 = j * kKeys;
-        const bool full = (mk[0] & mk[1] & mk[2] & mk[3]) == 0xFFFFFFFFu && k0 + kKeys <= row_end;
-        const bool warp_full = __all_sync(0xffffffffu, full);
-        if (kDebug) debug_row_scores(p, s_col, mk, k0, row_end, item);
-        if (!__all_sync(0xffffffffu, m >= m_safe)) {
-          // ---- max pass (first tiles of a row, or scores too large for a fixed m).
-          // S(j) ready implies the PV of tile j-1 is done (it was issued before the
-          // QK of tile j), so O may be rescaled here.
-          const float mx = warp_full ? row_tile_max<false>(s_col, mk, k0, row_end)
-                                     : row_tile_max<true>(s_col, mk, k0, row_end);
+        const bool full_a = (mk[0] & mk[1]) == 0xFFFFFFFFu && k0 + 64 <= row_end;
+        const bool full_b = (mk[2] & mk[3]) == 0xFFFFFFFFu && k0 + kKeys <= row_end;
+        const bool wfa = __all_sync(0xffffffffu, full_a);
+        const bool wfb = __all_sync(0xffffffffu, full_b);
+        const bool max_pass = !__all_sync(0xffffffffu, m >= m_safe);
+        bool have_b = false;
+        if (kDebug || max_pass) {
+          // Both halves' scores are needed first.  S of half B ready also means the
+          // PV of tile g-1 is done (it was issued before that QK), so O may be
+          // rescaled here.
+          if (!mbar_wait_warp(&sm.s_full[t][1], g & 1, abort, p.err)) {
+            ab = true;
+            break;
+          }
+          tc::fence_after_sync();
+          have_b = true;
+          if (kDebug) debug_row_scores(p, s_col, mk, k0, row_end, item);
+        }
+        if (max_pass) {
+          // ---- max pass (first tiles of a row, or scores too large for a fixed m)
+          const float mx = (wfa && wfb) ? row_tile_max<false>(s_col, mk, k0, row_end)
+                                        : row_tile_max<true>(s_col, mk, k0, row_end);
           const float mt = (mx == -INFINITY) ? -INFINITY : mx * cabs;
           const bool need = mt > m + kTauS;
           const bool resc = need && (m != -INFINITY);
           const float alpha = resc ? ex2_approx((m - mt) * kLog2e) : 1.f;
-          if (need) m = mt;
+          if (need) {
+            m = mt;
+            s_m = (int)mx;
+          }
           l *= alpha;
           if (__any_sync(0xffffffffu, resc)) rescale_row(o_col, alpha);
         }
-        // ---- P pass, one warpgroup at a time: the two Q tiles take turns so each P
-        // pass has the SM's exponential units to itself while the tensor core runs
-        // the other tile's MMAs.  Turn g of warpgroup 0 follows turn g-1 of
-        // warpgroup 1, turn g of warpgroup 1 follows turn g of warpgroup 0.
-        if (!mbar_wait_warp(&sm.turn[t], t == 0 ? ((g & 1) ^ 1) : (g & 1), abort, p.err)) {
-          ab = true;
-          break;
-        }
         // Once m >= m_safe every score is <= head_dim * |inv_sqrt_d| <= m + 11, so
         // P <= 2^15.9 fits f16 and the running max never has to move again.
-        const float bias = (m == -INFINITY) ? 0.f : -m * kLog2e;
-        l += warp_full ? row_tile_p<false>(s_col, mk, k0, row_end, k2, bias)
-                       : row_tile_p<true>(s_col, mk, k0, row_end, k2, bias);
+        PExp x;
+        x.k2 = k2;
+        x.bias = -(float)s_m * k2;
+        x.c = 8388608.f + (float)(16384 - 64 * s_m + 4 * lane);
+        x.a = tab_addr - 0x4B000000u;
+        // ---- half A: keys 0-63, P over S columns 0-31
+        l += wfa ? row_half_p<false>(s_col, mk, 0, k0, row_end, x) : row_half_p<true>(s_col, mk, 0, k0, row_end, x);
         tc::st_wait();
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&sm.turn[t ^ 1]);
-          mbar_arrive(&sm.p_full[t]);
+        if (lane == 0) mbar_arrive(&sm.p_full[t][0]);
+        // ---- half B: keys 64-127, P over S columns 64-95
+        if (!have_b) {
+          if (!mbar_wait_warp(&sm.s_full[t][1], g & 1, abort, p.err)) {
+            ab = true;
+            break;
+          }
+          tc::fence_after_sync();
         }
+        l += wfb ? row_half_p<false>(s_col + 64, mk, 4, k0, row_end, x)
+                 : row_half_p<true>(s_col + 64, mk, 4, k0, row_end, x);
+        tc::st_wait();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_full[t][1]);
         ++kvit;
       }
       if (ab) break;
