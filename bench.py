@@ -16,9 +16,9 @@ collective; --gather adds the output all-gather as a separate measurement).
 Timing: W untimed warm-up steps; L2 flushed (256 MiB write) before every timed
 step unless the inputs are larger than twice the L2; each step bracketed by CUDA
 events on the launch stream; the K steps bracketed by a barrier and
-torch.cuda.synchronize() on both sides; the max over ranks is reported.  `e2e` repeats the step through the public Python API with
-pinned host inputs: H2D copies, the forward and the D2H copy of O are inside the
-timed region.  `cpu_baseline` times the CPU oracle (the C restatement of the
+torch.cuda.synchronize() on both sides; the max over ranks is reported.  `e2e`
+repeats the step through the public Python API with pinned host inputs: H2D
+copies, the forward and the D2H copy of O are inside the timed region.  `cpu_baseline` times the CPU oracle (the C restatement of the
 reference algorithm) on a bounded sample on this host's cores.
 
 `--impl reference` times the reference's own CPU path for this forward: the
@@ -119,11 +119,11 @@ class ClockSampler:
 # ---------------------------------------------------------------------------- workloads
 def build_workload(name, rank, world, device):
     from hyperion_b200 import workloads as W
+    from hyperion_b200.sharding import head_range
 
     if name == "longctx":
         H = W.CONFIGS["longctx"]["H"]
-        per = H // world
-        heads = range(rank * per, (rank + 1) * per)
+        heads = head_range(H, world, rank)
         wk = W.make_config("longctx", device=device, exact=False, heads=heads, seed=rank)
         desc = f"longctx B1 H{H} S_q=S_kv=32768 D128 causal, heads {heads.start}-{heads.stop - 1} on this rank"
         return wk, desc, "strong"

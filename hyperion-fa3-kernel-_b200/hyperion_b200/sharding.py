@@ -1,0 +1,97 @@
+"""(batch, head) sharding of the forward over ranks, one process per GPU.
+
+The forward's units are independent per (batch, head) row: a row reads only its own
+Q rows, its own keys (its block-table row) and writes only its own O rows
+(hyperion_fa3_production_final.py:342-354, :582-593).  Ranks therefore split the
+rows and each runs the forward on its share with no data exchange.  The one
+collective is an optional gather of O for a caller that wants the whole output on
+every rank; a tensor-parallel consumer keeps its head block instead.
+
+Heads are split in contiguous blocks (the first H % world ranks take one extra), so
+a rank's rows are the same head block in every batch entry.
+"""
+from __future__ import annotations
+
+from typing import List
+
+import torch
+
+from .workloads import Workload, dense_worklist
+
+
+def head_range(n_heads: int, world: int, rank: int) -> range:
+    """Contiguous block of heads owned by `rank`; blocks differ in size by at most one."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    base, extra = divmod(n_heads, world)
+    lo = rank * base + min(rank, extra)
+    return range(lo, lo + base + (1 if rank < extra else 0))
+
+
+def shard_bh(batch: int, n_heads: int, heads: range) -> torch.Tensor:
+    """(batch, head) row ids b*H + h of a head block, in (b, h) order (int64)."""
+    b = torch.arange(batch, dtype=torch.int64).repeat_interleave(len(heads))
+    h = torch.tensor(list(heads), dtype=torch.int64).repeat(batch)
+    return b * n_heads + h
+
+
+def shard_workload(wk: Workload, heads: range) -> Workload:
+    """The rows of `heads` of a workload, as a workload of its own.
+
+    Q, context lengths, per-(batch, head) V scales and block-table rows are sliced;
+    a paged pool stays whole (the table rows point into it), a contiguous cache is
+    cut to the selected rows.  The worklist is rebuilt over the local rows."""
+    H = wk.heads
+    rows = shard_bh(wk.batch, H, heads).to(wk.q.device)
+    nb = len(rows)
+    q = wk.q.view(wk.n_bh, wk.seq_q, -1)[rows].reshape(nb * wk.seq_q, -1)
+    ctx = wk.ctx_lens[rows]
+    vs = wk.v_scale
+    if vs.numel() == wk.n_bh:
+        vs = vs[rows]
+    elif vs.numel() == H:
+        vs = vs[torch.tensor(list(heads), dtype=torch.int64, device=vs.device)]
+    if wk.block_tables.numel():
+        bt = wk.block_tables.view(wk.n_bh, -1)[rows].contiguous()
+        k, v = wk.k, wk.v
+    else:
+        span = wk.num_blocks * wk.block_size
+        k = wk.k.view(wk.n_bh, span, -1)[rows].reshape(nb * span, -1)
+        v = wk.v.view(wk.n_bh, span, -1)[rows].reshape(nb * span, -1)
+        bt = wk.block_tables
+    wl = dense_worklist(nb, wk.seq_q, wk.q.device)
+    if wk.seq_q == 1:
+        wl[:, 0] = 0
+    return Workload(name=f"{wk.name}[heads {heads.start}-{heads.stop - 1}]", worklist=wl, q=q.contiguous(),
+                    k=k.contiguous(), v=v.contiguous(), v_scale=vs.contiguous(), ctx_lens=ctx.contiguous(),
+                    block_tables=bt, seq_q=wk.seq_q, head_dim=wk.head_dim, block_size=wk.block_size,
+                    num_blocks=wk.num_blocks, causal=wk.causal, o_dtype=wk.o_dtype, batch=wk.batch,
+                    heads=len(heads), inv_sqrt_d=wk.inv_sqrt_d, meta=dict(wk.meta))
+
+
+def assemble_heads(parts: List[torch.Tensor], batch: int, n_heads: int, seq_q: int, world: int) -> torch.Tensor:
+    """Full O [batch*H*seq_q, D] from the ranks' head-block outputs, in rank order."""
+    d = parts[0].shape[-1]
+    out = torch.empty(batch, n_heads, seq_q, d, dtype=parts[0].dtype, device=parts[0].device)
+    for r, part in enumerate(parts):
+        hr = head_range(n_heads, world, r)
+        out[:, hr.start:hr.stop] = part.reshape(batch, len(hr), seq_q, d)
+    return out.reshape(batch * n_heads * seq_q, d)
+
+
+def gather_output(o_local: torch.Tensor, batch: int, n_heads: int, seq_q: int, group=None) -> torch.Tensor:
+    """All-gathers the head-block outputs of every rank into the full O on each rank.
+
+    Blocks of unequal size are padded to the largest for the collective.  Every rank
+    of `group` must call this with its own block, in the same order of collectives."""
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    d = o_local.shape[-1]
+    rows_max = batch * len(head_range(n_heads, world, 0)) * seq_q
+    buf = torch.zeros(rows_max, d, dtype=o_local.dtype, device=o_local.device)
+    buf[: o_local.shape[0]] = o_local
+    bufs = [torch.empty_like(buf) for _ in range(world)]
+    dist.all_gather(bufs, buf, group=group)
+    parts = [bufs[r][: batch * len(head_range(n_heads, world, r)) * seq_q] for r in range(world)]
+    return assemble_heads(parts, batch, n_heads, seq_q, world)
