@@ -18,8 +18,9 @@ step unless the inputs are larger than twice the L2; each step bracketed by CUDA
 events on the launch stream; the K steps bracketed by a barrier and
 torch.cuda.synchronize() on both sides; the max over ranks is reported.  `e2e`
 repeats the step through the public Python API with pinned host inputs: H2D
-copies, the forward and the D2H copy of O are inside the timed region.  `cpu_baseline` times the CPU oracle (the C restatement of the
-reference algorithm) on a bounded sample on this host's cores.
+copies, the forward and the D2H copy of O are inside the timed region.
+`cpu_baseline` times the CPU oracle (the C restatement of the reference
+algorithm) on a bounded sample on this host's cores.
 
 `--impl reference` times the reference's own CPU path for this forward: the
 reference's kernel does not build and has no CPU attention, so that is the C
@@ -426,7 +427,7 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": total_ms_max / args.steps, "higher_is_better": True,
             "scaling": scaling, "vs_baseline": None,
             "dtype": "sign-bit QK (e4m3 +-1 MMA, exact int) / f16 PV" if info["path"] == "tile"
-                     else "sign-bit QK (popc, exact int) / f32 PV",
+                     else "sign-bit QK (popc, exact int) / f16x2 PV products, f32 accumulation",
             "data": "synthetic: seeded random sign bits for Q/K, N(0,1) V as FP8 e4m3 with per-head scale",
             "config": c, "pairs_per_step": pairs_all,
             "roofline": roof, "cpu_baseline": cpu,
