@@ -40,39 +40,6 @@ __device__ __forceinline__ void mma_f8f6f4_ss(uint32_t d_tmem, uint64_t adesc, u
       : "memory");
 }
 
-// The same MMAs with the descriptors given as 32-bit halves (the low word holds
-// the start address, so advancing a descriptor is one 32-bit add) and the
-// accumulate flag as a compile-time constant.
-// Executed by a whole warp with warp-uniform operands (so they can stay in the
-// uniform datapath); only the lane with `leader` != 0 issues the MMA.
-template <int kAccumulate>
-__device__ __forceinline__ void mma_f8f6f4_ss_lohi(uint32_t leader, uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi,
-                                                   uint32_t b_lo, uint32_t b_hi, uint32_t idesc) {
-  asm volatile(
-      "{\n\t.reg .b64 ad, bd;\n\t.reg .pred p, l;\n\t"
-      "mov.b64 ad, {%2, %3};\n\tmov.b64 bd, {%4, %5};\n\tsetp.ne.b32 p, %7, 0;\n\tsetp.ne.b32 l, %0, 0;\n\t"
-      "@l tcgen05.mma.cta_group::1.kind::f8f6f4 [%1], ad, bd, %6, p;\n\t}\n" ::"r"(leader),
-      "r"(d_tmem), "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "n"(kAccumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_f16_ts_lohi(uint32_t leader, uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo,
-                                                uint32_t b_hi, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .b64 bd;\n\t.reg .pred p, l;\n\t"
-      "mov.b64 bd, {%3, %4};\n\tsetp.ne.b32 p, %6, 0;\n\tsetp.ne.b32 l, %0, 0;\n\t"
-      "@l tcgen05.mma.cta_group::1.kind::f16 [%1], [%2], bd, %5, p;\n\t}\n" ::"r"(leader),
-      "r"(d_tmem), "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// tcgen05.commit issued by the leader lane only.
-__device__ __forceinline__ void commit_leader(uint32_t leader, uint64_t* bar) {
-  asm volatile(
-      "{\n\t.reg .pred l;\n\tsetp.ne.b32 l, %0, 0;\n\t"
-      "@l tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%1];\n\t}\n" ::"r"(leader),
-      "r"(smem_u32(bar))
-      : "memory");
-}
-
 // D[tmem] (+)= A[tmem] * B[smem], f16/bf16 operands, f32 accumulate.
 __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
                                            uint32_t accumulate) {
@@ -157,15 +124,6 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr, uint32_t lbo,
   d |= (uint64_t)1 << 46;
   d |= (uint64_t)2 << 61;
   return d;
-}
-
-// Low / high 32-bit words of sw128_desc: lo = start/16 | (lbo/16) << 16,
-// hi = sbo/16 | version 1 | layout 128B swizzle.
-__host__ __device__ constexpr uint32_t sw128_lo(uint32_t smem_addr, uint32_t lbo) {
-  return ((smem_addr >> 4) & 0x3FFFu) | (((lbo >> 4) & 0x3FFFu) << 16);
-}
-__host__ __device__ constexpr uint32_t sw128_hi(uint32_t sbo) {
-  return ((sbo >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
 }
 
 // Instruction descriptor: f32 accumulator, dense, M = 128, N given, operand
