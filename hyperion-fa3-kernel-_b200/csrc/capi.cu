@@ -18,6 +18,7 @@
 #include "common.cuh"
 #include "row_kernel.cuh"
 #include "tile_kernel.cuh"
+#include "kv_write.cuh"
 
 namespace {
 
@@ -338,6 +339,55 @@ int hyperion_read_device_errors(void* workspace, size_t workspace_bytes, void* s
 }
 
 }  // extern "C"
+
+extern "C" int hyperion_kv_cache_write(const void* K_new, const void* V_new, int32_t in_dtype, int32_t n_tokens,
+                                       int32_t n_heads, int32_t head_dim, const int32_t* seq_ids,
+                                       const int32_t* positions, const int32_t* block_tables,
+                                       int64_t block_tables_numel, int32_t block_size, int32_t num_blocks,
+                                       const float* V_scale, int64_t v_scale_numel, uint32_t* K_cache,
+                                       uint8_t* V_cache, int64_t pool_rows, void* workspace, size_t workspace_bytes,
+                                       void* stream) {
+  if (in_dtype != HYPERION_DTYPE_F16 && in_dtype != HYPERION_DTYPE_BF16 && in_dtype != HYPERION_DTYPE_F32)
+    return fail(HYPERION_ERR_INVALID_ARG, "in_dtype is not F16, BF16 or F32");
+  if (head_dim != 128 && head_dim != 256) return fail(HYPERION_ERR_UNSUPPORTED, "head_dim must be 128 or 256");
+  if (n_tokens < 0) return fail(HYPERION_ERR_INVALID_ARG, "n_tokens < 0");
+  if (n_heads < 1) return fail(HYPERION_ERR_INVALID_ARG, "n_heads < 1");
+  if (block_size < 1 || num_blocks < 1) return fail(HYPERION_ERR_INVALID_ARG, "block_size and num_blocks must be >= 1");
+  if (v_scale_numel < 1) return fail(HYPERION_ERR_INVALID_ARG, "V_scale is empty");
+  if (pool_rows < 1) return fail(HYPERION_ERR_INVALID_ARG, "pool_rows < 1");
+  if (block_tables_numel < 0 || (block_tables_numel > 0 && block_tables == nullptr))
+    return fail(HYPERION_ERR_INVALID_ARG, "block_tables is NULL but numel > 0");
+  if (workspace == nullptr || workspace_bytes < hyp::kWsPartials ||
+      reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+    return fail(HYPERION_ERR_WORKSPACE, "workspace missing, smaller than 256 bytes or not 256-byte aligned");
+  if (n_tokens == 0) return HYPERION_OK;
+  if (!K_new || !V_new || !seq_ids || !positions || !V_scale || !K_cache || !V_cache)
+    return fail(HYPERION_ERR_INVALID_ARG, "a tensor pointer is NULL");
+  if (reinterpret_cast<uintptr_t>(K_cache) % 16 != 0) return fail(HYPERION_ERR_INVALID_ARG, "K_cache must be 16-byte aligned");
+  const size_t esz = in_dtype == HYPERION_DTYPE_F32 ? 4 : 2;
+  if (reinterpret_cast<uintptr_t>(K_new) % esz != 0 || reinterpret_cast<uintptr_t>(V_new) % esz != 0)
+    return fail(HYPERION_ERR_INVALID_ARG, "K_new / V_new are not aligned to their element size");
+  hyp::kvw::Args a;
+  a.k_new = K_new;
+  a.v_new = V_new;
+  a.n_tokens = n_tokens;
+  a.n_heads = n_heads;
+  a.seq_ids = seq_ids;
+  a.positions = positions;
+  a.block_tables = block_tables_numel > 0 ? block_tables : nullptr;
+  a.bt_rows = block_tables_numel / num_blocks;
+  a.block_size = block_size;
+  a.num_blocks = num_blocks;
+  a.v_scale = V_scale;
+  a.v_scale_numel = v_scale_numel;
+  a.k_cache = K_cache;
+  a.v_cache = V_cache;
+  a.pool_rows = pool_rows;
+  a.err = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + hyp::kWsError);
+  const cudaError_t e = hyp::kvw::launch(a, head_dim, in_dtype, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cache writer launch");
+  return HYPERION_OK;
+}
 
 // ---------------------------------------------------------------------------
 // The forward for callers that cannot allocate device memory.

@@ -187,6 +187,54 @@ def hyperion_apex_kernel(
         raise RuntimeError(f"hyperion_apex_kernel failed (status {rc}): {_capi.last_error()}")
 
 
+def kv_cache_write(K_new: torch.Tensor, V_new: torch.Tensor, seq_ids: torch.Tensor, positions: torch.Tensor,
+                   block_tables: Optional[torch.Tensor], block_size: int, num_blocks: int, V_scale: torch.Tensor,
+                   K_cache: torch.Tensor, V_cache: torch.Tensor) -> None:
+    """Writes new keys and values into the cache the forward reads (asynchronous on
+    the current stream of K_cache's device).
+
+    K_new, V_new: [n_tokens, n_heads, head_dim] float16 / bfloat16 / float32; token i
+    belongs to sequence seq_ids[i] (int32) at position positions[i] (int32).  Each
+    (token, head) row lands in the slot the forward reads it from (block_tables row
+    seq*n_heads + head, or the contiguous layout when block_tables is None / empty):
+    K as sign bits into K_cache [pool_rows, head_dim/32] (int32 / uint32 storage), V
+    as e4m3 codes of clamp(v / scale, -448, 448) into V_cache [pool_rows, head_dim]
+    uint8, scale V_scale[0] or V_scale[(seq*n_heads + head) % numel].  Rows whose
+    position or page falls outside the pool are skipped and flagged
+    (read_device_errors)."""
+    dtypes = {torch.float16: _capi.DTYPE_F16, torch.bfloat16: _capi.DTYPE_BF16, torch.float32: _capi.DTYPE_F32}
+    _check(K_cache.is_cuda and K_cache.is_contiguous(), "K_cache must be a contiguous CUDA tensor")
+    dev = K_cache.device
+    for name, t in (("K_new", K_new), ("V_new", V_new), ("seq_ids", seq_ids), ("positions", positions),
+                    ("V_scale", V_scale), ("V_cache", V_cache)):
+        _check(t.is_cuda and t.device == dev and t.is_contiguous(), f"{name} must be a contiguous tensor on {dev}")
+    _check(K_new.dtype in dtypes and V_new.dtype == K_new.dtype, "K_new / V_new must share a float16, bfloat16 or "
+                                                                  "float32 dtype")
+    _check(K_new.dim() == 3 and V_new.shape == K_new.shape, "K_new / V_new must be [n_tokens, n_heads, head_dim]")
+    n_tokens, n_heads, head_dim = K_new.shape
+    _check(head_dim in (128, 256), "head_dim must be 128 or 256")
+    _check(seq_ids.dtype == torch.int32 and positions.dtype == torch.int32 and seq_ids.numel() == n_tokens
+           and positions.numel() == n_tokens, "seq_ids / positions must be int32 [n_tokens]")
+    _check(V_scale.dtype == torch.float32 and V_scale.numel() >= 1, "V_scale must be a non-empty float32 tensor")
+    _check(V_cache.element_size() == 1 and V_cache.numel() % head_dim == 0, "V_cache must be uint8 [pool_rows, head_dim]")
+    pool_rows = V_cache.numel() // head_dim
+    _check(_nbytes(K_cache) >= pool_rows * head_dim // 8, "K_cache smaller than pool_rows rows of head_dim/8 bytes")
+    bt_numel = 0
+    if block_tables is not None and block_tables.numel() > 0:
+        _check(block_tables.is_cuda and block_tables.device == dev and block_tables.is_contiguous()
+               and block_tables.dtype == torch.int32, "block_tables must be a contiguous int32 CUDA tensor")
+        bt_numel = block_tables.numel()
+    with torch.cuda.device(dev):
+        ws = _workspace(dev, 1 << 16)
+        rc = _capi.lib.hyperion_kv_cache_write(
+            K_new.data_ptr(), V_new.data_ptr(), dtypes[K_new.dtype], n_tokens, n_heads, head_dim,
+            seq_ids.data_ptr(), positions.data_ptr(), block_tables.data_ptr() if bt_numel else None, bt_numel,
+            int(block_size), int(num_blocks), V_scale.data_ptr(), V_scale.numel(), K_cache.data_ptr(),
+            V_cache.data_ptr(), pool_rows, ws.data_ptr(), ws.numel(), torch.cuda.current_stream(dev).cuda_stream)
+    if rc != _capi.HYPERION_OK:
+        raise RuntimeError(f"kv_cache_write failed (status {rc}): {_capi.last_error()}")
+
+
 def hyperion_reset_counter(*, grid=None, block=None, device=None) -> None:
     """Reference call site hyperion_fa3_production_final.py:905.  Zeroes the work
     counter of the current device's workspace on the current stream.  The forward

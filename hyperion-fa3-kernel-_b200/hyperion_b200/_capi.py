@@ -45,6 +45,7 @@ EXPORTED = (
     "hyperion_last_error_string",
     "hyperion_version",
     "hyperion_apex_kernel_noalloc",
+    "hyperion_kv_cache_write",
 )
 
 # Fixed per-device scratch of hyperion_apex_kernel_noalloc (HYPERION_NOALLOC_SCRATCH_BYTES).
@@ -115,6 +116,10 @@ def _load() -> ctypes.CDLL:
     lib.hyperion_version.argtypes = []
     lib.hyperion_apex_kernel_noalloc.restype = ctypes.c_int
     lib.hyperion_apex_kernel_noalloc.argtypes = _FWD_ARGS + [_vp]
+    _i64 = ctypes.c_int64
+    lib.hyperion_kv_cache_write.restype = ctypes.c_int
+    lib.hyperion_kv_cache_write.argtypes = [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _i64, _i32, _i32, _vp, _i64,
+                                            _vp, _vp, _i64, _vp, ctypes.c_size_t, _vp]
     return lib
 
 

@@ -160,6 +160,28 @@ const char* hyperion_last_error_string(void);
 /* Library version as major*10000 + minor*100 + patch. */
 int32_t hyperion_version(void);
 
+/* Writes new keys and values into the cache format the forward reads.  It has no
+ * counterpart in the reference, whose engine allocates the paged pool
+ * (hyperion_fa3_production_final.py:1017-1032) but has no kernel that fills it.
+ * K_new, V_new: [n_tokens, n_heads, head_dim] of in_dtype (HYPERION_DTYPE_*).
+ * Token i belongs to sequence seq_ids[i] at position positions[i]; its row for head
+ * h (bh = seq_ids[i]*n_heads + h) goes to the slot the forward reads it from:
+ * block_tables[bh*num_blocks + pos/block_size]*block_size + pos%block_size (or the
+ * contiguous slot bh*num_blocks*block_size + pos when block_tables_numel is 0).
+ * K: sign bits (1 where k >= 0) into K_cache [pool_rows, head_dim/32] uint32;
+ * V: e4m3 codes of clamp(v / scale, -448, 448), round to nearest even, into V_cache
+ * [pool_rows, head_dim] uint8, with scale V_scale[0] (numel 1) or V_scale[bh % numel].
+ * Positions or page ids outside the pool set HYPERION_DEVERR_BAD_ITEM / _BAD_BLOCK in
+ * the workspace error word and that row is skipped.  Asynchronous on `stream`. */
+int hyperion_kv_cache_write(const void* K_new, const void* V_new, int32_t in_dtype,
+                            int32_t n_tokens, int32_t n_heads, int32_t head_dim,
+                            const int32_t* seq_ids, const int32_t* positions,
+                            const int32_t* block_tables, int64_t block_tables_numel,
+                            int32_t block_size, int32_t num_blocks,
+                            const float* V_scale, int64_t v_scale_numel,
+                            uint32_t* K_cache, uint8_t* V_cache, int64_t pool_rows,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
 /* Fixed scratch of hyperion_apex_kernel_noalloc, per device, in bytes. */
 #define HYPERION_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
 
