@@ -6,6 +6,9 @@
 // work stealing, hyperion_fa3_production_final.py:236-243, :332-336), longest
 // causal rows first.  The unit's keys are walked in 128-key tiles:
 //
+//   scheduler warp takes the tickets and prepares each unit (segments of the chunk,
+//                  context length, tile count; all dependent global reads) one
+//                  unit ahead of the other roles, in a 2-slot ring;
 //   loader warp    cp.async.bulk of the raw page pieces (sign bits 16 B/key, FP8
 //                  codes 128 B/key) into a 2-stage ring, with the key-valid mask
 //                  (context length, page ids inside the pool; :402-411, :479-486);
@@ -29,9 +32,9 @@
 // first 32 columns of that half's S.  The QK of half A of tile g+1 only has to wait
 // for the PV of half A of tile g, so it runs on the tensor core while the softmax
 // is still on half B of tile g: the next scores are ready when the softmax wants
-// them, and the two Q tiles' softmax passes overlap each other.  Every mbarrier wait is bounded; on a timeout the CTA
-// raises HYPERION_DEVERR_WAIT_TIMEOUT, lets in-flight copies and MMAs land,
-// frees TMEM and exits.
+// them, and the two Q tiles' softmax passes overlap each other.  Every mbarrier
+// wait is bounded; on a timeout the CTA raises HYPERION_DEVERR_WAIT_TIMEOUT, lets
+// in-flight copies and MMAs land, frees TMEM and exits.
 #pragma once
 
 #include "common.cuh"
@@ -50,8 +53,9 @@ constexpr int kMmaWarp = 8;  // warps 8 and 9: the MMA issuers of Q tiles 0 and 
 constexpr int kLoadWarp = 10;
 constexpr int kConvWarp0 = 11;
 constexpr int kConvWarps = 4;
-constexpr int kThreads = 32 * (kConvWarp0 + kConvWarps);  // 480
-constexpr int kSchedConsumers = 4 * kQTiles + kQTiles + kConvWarps;  // warps that read each unit
+constexpr int kSchedWarp = kConvWarp0 + kConvWarps;  // 15
+constexpr int kThreads = 32 * (kSchedWarp + 1);        // 512
+constexpr int kSchedConsumers = 4 * kQTiles + kQTiles + kConvWarps + 1;  // warps that read each unit
 constexpr uint32_t kTmemCols = 512;
 constexpr int kKTileBytes = kKeys * 128;      // e4m3 +-1, K-major SW128
 constexpr int kVTileBytes = kKeys * 256;      // f16, MN-major SW128: two 64-dim blocks
@@ -420,10 +424,9 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
   const uint32_t tmem = sm.tmem_base;
   volatile int* abort = &sm.abort;
 
-  if (warp == kLoadWarp) {
-    // ================================================================ loader
-    const uint64_t pol = policy_evict_last();
-    uint32_t uc = 0, rit = 0;
+  if (warp == kSchedWarp) {
+    // ================================================================ scheduler
+    uint32_t uc = 0;
     const long long cap = (long long)p.num_blocks * p.block_size;
     // Ticket order: in a (bh, q_idx)-ordered worklist chunk c holds q rows
     // [256*(c % cpb), ...) of its bh, and causal cost grows with that position.
@@ -435,6 +438,10 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     const int n_tickets = groups * cpb;
     bool stop = false;
     while (!stop) {
+      // Take the next ticket only once every role has started the previous unit:
+      // the metadata of unit uc is then ready one unit ahead, and no CTA holds a
+      // ticket it will not start soon (the tail stays balanced).
+      if (uc >= 1 && !mbar_wait_warp(&sm.sched_empty[(uc - 1) & 1], ((uc - 1) >> 1) & 1, abort, p.err)) break;
       int c = -1;
       for (;;) {
         int t = 0;
@@ -518,6 +525,25 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           mbar_arrive(&sm.sched_full[uc & 1]);
         }
         ++uc;
+        seg_lo = seg_hi;
+      }
+    }
+  } else if (warp == kLoadWarp) {
+    // ================================================================ loader
+    const uint64_t pol = policy_evict_last();
+    uint32_t uc = 0, rit = 0;
+    bool stop = false;
+    while (!stop) {
+      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) break;
+      const UnitInfo u = sm.unit[uc & 1];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.sched_empty[uc & 1]);
+      ++uc;
+      if (u.kind == 0) break;
+      {
+        const int bh0 = u.bh;
+        const int kv_len = u.kv_len;
+        const int n_tiles = u.n_tiles;
         for (int j = 0; j < n_tiles; ++j) {
           const int r = rit % kRawStages;
           if (!mbar_wait_warp(&sm.raw_empty[r], ((rit / kRawStages) & 1) ^ 1, abort, p.err)) {
@@ -576,15 +602,13 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           }
           ++rit;
         }
-        if (stop) break;
-        seg_lo = seg_hi;
       }
     }
     if (*abort && lane == 0) {
       for (uint32_t i = (rit > (uint32_t)kRawStages ? rit - kRawStages : 0u); i < rit; ++i)
         mbar_drain(&sm.raw_full[i % kRawStages], (i / kRawStages) & 1);
     }
-  } else if (warp >= kConvWarp0) {
+  } else if (warp >= kConvWarp0 && warp < kConvWarp0 + kConvWarps) {
     // ================================================================ converters
     const int ct = threadIdx.x - 32 * kConvWarp0;  // 0..127
     uint32_t uc = 0, rit = 0, kvit = 0, uq = 0;
