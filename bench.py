@@ -18,7 +18,9 @@ step unless the inputs are larger than twice the L2; each step bracketed by CUDA
 events on the launch stream; the K steps bracketed by a barrier and
 torch.cuda.synchronize() on both sides; the max over ranks is reported.  `e2e`
 repeats the step through the public Python API with pinned host inputs: H2D
-copies, the forward and the D2H copy of O are inside the timed region.
+copies, the forward and the D2H copy of O are inside the timed region (decode
+keeps the KV cache resident and writes each step's new token into it; prefill
+pipelines its copies over two streams).
 `cpu_baseline` times the CPU oracle (the C restatement of the reference
 algorithm) on a bounded sample on this host's cores.
 
@@ -275,6 +277,109 @@ def run_reference(args):
     return 0
 
 
+def run_e2e(hyperion, wk, o, args, barrier):
+    """Times args.steps steps through the public Python API with pinned host buffers;
+    returns (total ms, H2D bytes per step, D2H bytes per step, description).
+
+    Decode (one query row): the KV cache stays on the device, as the reference's
+    engine keeps it (hyperion_fa3_production_final.py:1017-1032).  A step copies in
+    the new token's Q rows, K and V (bf16 [batch, heads, D]), positions and context
+    lengths, writes K and V into the cache (kv_cache_write), runs the forward and
+    copies O out.
+    Prefill: a step copies in all of the forward's inputs and copies O out.  Steps
+    are pipelined: the inputs of step i+1 go in and the O of step i-1 comes out
+    while step i computes (copy streams, double buffers; forwards stay in order on
+    one stream, since they share the workspace)."""
+    dev = o.device
+    main = torch.cuda.current_stream(dev)
+    if wk.seq_q == 1:
+        B, H, D = wk.batch, wk.heads, wk.head_dim
+        ctx = wk.ctx_lens.view(B, H)[:, 0].to(torch.int32)
+        g = torch.Generator().manual_seed(5)
+        host = {
+            "q": wk.q.cpu().pin_memory(),
+            "k_new": torch.randn(B, H, D, generator=g).to(torch.bfloat16).pin_memory(),
+            "v_new": torch.randn(B, H, D, generator=g).to(torch.bfloat16).pin_memory(),
+            "seq_ids": torch.arange(B, dtype=torch.int32).pin_memory(),
+            "positions": (ctx - 1).clamp_min(0).cpu().pin_memory(),
+            "ctx_lens": wk.ctx_lens.cpu().pin_memory(),
+        }
+        dbuf = {k: torch.empty_like(t, device=dev) for k, t in host.items()}
+        o_host = torch.empty(o.shape, dtype=o.dtype).pin_memory()
+
+        def step():
+            for k_, t in host.items():
+                dbuf[k_].copy_(t, non_blocking=True)
+            hyperion.kv_cache_write(dbuf["k_new"], dbuf["v_new"], dbuf["seq_ids"], dbuf["positions"],
+                                    wk.block_tables, wk.block_size, wk.num_blocks, wk.v_scale, wk.k, wk.v)
+            sub = type(wk)(**{**wk.__dict__, "q": dbuf["q"], "ctx_lens": dbuf["ctx_lens"]})
+            call_forward(hyperion, sub, o, path=args.path)
+            o_host.copy_(o, non_blocking=True)
+
+        step()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(main)
+        for _ in range(args.steps):
+            step()
+        e1.record(main)
+        torch.cuda.synchronize()
+        barrier()
+        h2d = sum(t.numel() * t.element_size() for t in host.values())
+        mode = ("resident KV cache: per step H2D of Q, the new token's K/V (bf16), positions and context lengths; "
+                "kv_cache_write; forward; D2H of O")
+        return e0.elapsed_time(e1), h2d, o_host.numel() * o_host.element_size(), mode
+
+    keys = ("worklist", "q", "k", "v", "v_scale", "ctx_lens", "block_tables")
+    host = {k: getattr(wk, k).cpu().pin_memory() for k in keys}
+    dbufs = [{k: torch.empty_like(getattr(wk, k)) for k in keys} for _ in range(2)]
+    outs = [o, torch.empty_like(o)]
+    o_hosts = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for _ in range(2)]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    in_done = [torch.cuda.Event() for _ in range(2)]    # inputs of buffer b are on the device
+    fwd_done = [torch.cuda.Event() for _ in range(2)]   # the forward has read buffer b and written O b
+    out_done = [torch.cuda.Event() for _ in range(2)]   # O b has reached the host
+
+    def issue(i):
+        b = i % 2
+        with torch.cuda.stream(s_in):
+            if i >= 2:
+                s_in.wait_event(fwd_done[b])
+            for k_ in keys:
+                dbufs[b][k_].copy_(host[k_], non_blocking=True)
+            in_done[b].record(s_in)
+        main.wait_event(in_done[b])
+        if i >= 2:
+            main.wait_event(out_done[b])
+        sub = type(wk)(**{**wk.__dict__, **dbufs[b]})
+        call_forward(hyperion, sub, outs[b], path=args.path)
+        fwd_done[b].record(main)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(fwd_done[b])
+            o_hosts[b].copy_(outs[b], non_blocking=True)
+            out_done[b].record(s_out)
+
+    for i in range(2):
+        issue(i)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(main)
+    s_in.wait_event(e0)
+    for i in range(args.steps):
+        issue(i)
+    main.wait_stream(s_out)
+    e1.record(main)
+    torch.cuda.synchronize()
+    barrier()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    mode = "all inputs H2D and O D2H every step, pipelined over two copy streams"
+    return e0.elapsed_time(e1), h2d, o_hosts[0].numel() * o_hosts[0].element_size(), mode
+
+
 def run_ours(args):
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -342,32 +447,7 @@ def run_ours(args):
     clk = clocks.stop() if rank == 0 else None
 
     # e2e through the public API with pinned host buffers.
-    host = {k: getattr(wk, k).cpu().pin_memory() for k in ("worklist", "q", "k", "v", "v_scale", "ctx_lens",
-                                                           "block_tables")}
-    dbuf = {k: torch.empty_like(getattr(wk, k)) for k in host}
-    o_host = torch.empty(o.shape, dtype=o.dtype).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
-    d2h = o_host.numel() * o_host.element_size()
-
-    def e2e_step():
-        for k_, t in host.items():
-            dbuf[k_].copy_(t, non_blocking=True)
-        sub = type(wk)(**{**wk.__dict__, **dbuf})
-        call_forward(hyperion, sub, o, path=args.path)
-        o_host.copy_(o, non_blocking=True)
-
-    e2e_step()
-    torch.cuda.synchronize()
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    e_start.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e_end.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    e2e_ms = e_start.elapsed_time(e_end)
+    e2e_ms, h2d, d2h, e2e_mode = run_e2e(hyperion, wk, o, args, barrier)
 
     gather_ms = None
     if args.gather and world > 1:
@@ -432,7 +512,7 @@ def run_ours(args):
             "config": c, "pairs_per_step": pairs_all,
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": "pairs/s", "h2d_bytes_per_step": h2d * world,
-                    "d2h_bytes_per_step": d2h * world},
+                    "d2h_bytes_per_step": d2h * world, "mode": e2e_mode},
             "gpu_launches": info["kernels"] * args.steps,
             "clocks": clk, "device_errors": errs,
             "step_ms_min": min(step_ms), "step_ms_max": max(step_ms),
