@@ -314,6 +314,39 @@ def test_tile_path_large_scores_force_rescale(hyperion, oracle):
     check(oracle, wk, o)
 
 
+@pytest.mark.parametrize("path", ["row", "tile"])
+def test_negative_inv_sqrt_d(hyperion, oracle, path):
+    # A negative scale turns the scores around: the tile path flips Q's bits, the row
+    # path takes the integer minimum as the group maximum.
+    wk = W.make_dense("n", 1, 2, 256, 512, causal=True, o_dtype=torch.float32, seed=27)
+    wk.inv_sqrt_d = -1.0 / 128 ** 0.5
+    o, err, dbg = run(hyperion, wk, path=path, debug_ld=512)
+    assert err == 0 and hyperion.last_call_info()["path"] == path
+    check(oracle, wk, o)
+    _, _, _, ref_scores = oracle.forward_workload_c(wk, scores_ld=512)
+    assert np.array_equal(dbg, ref_scores)  # the integer scores D - 2*popc, unscaled
+
+
+@pytest.mark.parametrize("path", ["row", "tile"])
+def test_shuffled_worklist(hyperion, oracle, path):
+    # Items in random order: every 256-item chunk mixes many (batch, head) rows, so the
+    # tile path runs many short segments per chunk.
+    wk = W.make_dense("s", 2, 3, 96, 96, causal=True, o_dtype=torch.float32, seed=28)
+    perm = torch.randperm(wk.total_work, generator=torch.Generator().manual_seed(9))
+    wk.worklist = wk.worklist[perm].contiguous()
+    o, err, _ = run(hyperion, wk, path=path)
+    assert err == 0 and hyperion.last_call_info()["path"] == path
+    check(oracle, wk, o)
+
+
+def test_row_path_large_scores_force_rescale(hyperion, oracle):
+    wk = W.make_dense("rr", 1, 2, 8, 3000, causal=False, o_dtype=torch.float32, seed=29)
+    wk.inv_sqrt_d = 1.0
+    o, err, _ = run(hyperion, wk, path="row", num_splits=3)
+    assert err == 0
+    check(oracle, wk, o)
+
+
 def test_tile_path_short_and_empty_contexts(hyperion, oracle):
     wk = W.make_dense("e", 1, 4, 256, 256, causal=False, o_dtype=torch.float32, seed=26)
     wk.ctx_lens[0] = 0
