@@ -227,6 +227,7 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   // Contiguous layout: page ids are bh * num_blocks + page; all of them are in the
   // pool when the pool holds n_bh * num_blocks pages.
   p.pages_all_valid = (!paged && (long long)ext->n_bh * num_blocks <= p.pool_blocks) ? 1 : 0;
+  p.o_align32 = (reinterpret_cast<uintptr_t>(O) % 32 == 0) ? 1 : 0;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.counters = reinterpret_cast<uint32_t*>(ws + hyp::kWsCounters);
   p.err = reinterpret_cast<uint32_t*>(ws + hyp::kWsError);

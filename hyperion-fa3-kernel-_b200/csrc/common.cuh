@@ -55,6 +55,7 @@ struct FwdParams {
   int* debug_scores;
   long long debug_ld;
   int pages_all_valid;  // 1: every page id the kernels can read is inside the pool (host-checked)
+  int o_align32;        // 1: O is 32-byte aligned, so a 16-value row piece is whole 32-byte sectors
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -150,38 +150,51 @@ __device__ __forceinline__ uint32_t sw128_off(uint32_t r, uint32_t c) {
   return (r >> 3) * 1024u + (r & 7u) * 128u + ((c ^ (r & 7u)) << 4);
 }
 
-// Stores 16 consecutive output values of one row (f32, bf16 or f16).
+// One 32-byte store (8 words), dst 32-byte aligned: a whole L2 sector per lane.
+__device__ __forceinline__ void st_global_v8(void* dst, const uint32_t (&w)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(w[0]), "r"(w[1]),
+               "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
+// Stores 16 consecutive output values of one row (f32, bf16 or f16).  With a
+// 32-byte aligned O (`sectors`) each 32 bytes go out as one store.
 template <int kDtype>
-__device__ __forceinline__ void store_row16(void* o, long long base, const float (&v)[16]) {
+__device__ __forceinline__ void store_row16(void* o, long long base, const float (&v)[16], bool sectors) {
+  uint32_t w[16];
+  constexpr int kWords = (kDtype == HYPERION_DTYPE_F32) ? 16 : 8;
   if constexpr (kDtype == HYPERION_DTYPE_F32) {
-    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(o) + base);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-  } else if constexpr (kDtype == HYPERION_DTYPE_BF16) {
-    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(o) + base);
+    for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(v[i]);
+  } else {
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      uint32_t w[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * i + 2 * k], v[8 * i + 2 * k + 1]);
-        w[k] = *reinterpret_cast<uint32_t*>(&h);
+    for (int i = 0; i < 8; ++i) {
+      if constexpr (kDtype == HYPERION_DTYPE_BF16) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        w[i] = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        w[i] = pack_f16x2(v[2 * i], v[2 * i + 1]);
       }
-      dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+  uint32_t* dst = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(o) + base * (kDtype == HYPERION_DTYPE_F32 ? 4 : 2));
+  if (sectors) {
+#pragma unroll
+    for (int j = 0; j < kWords; j += 8) {
+      const uint32_t piece[8] = {w[j], w[j + 1], w[j + 2], w[j + 3], w[j + 4], w[j + 5], w[j + 6], w[j + 7]};
+      st_global_v8(dst + j, piece);
     }
   } else {
-    uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(o) + base);
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      dst[i] = make_uint4(pack_f16x2(v[8 * i], v[8 * i + 1]), pack_f16x2(v[8 * i + 2], v[8 * i + 3]),
-                          pack_f16x2(v[8 * i + 4], v[8 * i + 5]), pack_f16x2(v[8 * i + 6], v[8 * i + 7]));
-    }
+    for (int j = 0; j < kWords; j += 4) d4[j / 4] = make_uint4(w[j], w[j + 1], w[j + 2], w[j + 3]);
   }
 }
 
 // Epilogue of one row: O = acc * scale from TMEM to global memory, 16 columns at a time.
 template <int kDtype>
-__device__ __forceinline__ void store_o_row(void* o, long long o_base, uint32_t o_col, float scale, bool row_ok) {
+__device__ __forceinline__ void store_o_row(void* o, long long o_base, uint32_t o_col, float scale, bool row_ok,
+                                            bool sectors) {
 #pragma unroll 1
   for (int c = 0; c < 8; ++c) {
     uint32_t v[16];
@@ -191,23 +204,23 @@ __device__ __forceinline__ void store_o_row(void* o, long long o_base, uint32_t 
       float f[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) f[i] = __uint_as_float(v[i]) * scale;
-      store_row16<kDtype>(o, o_base + 16 * c, f);
+      store_row16<kDtype>(o, o_base + 16 * c, f, sectors);
     }
   }
 }
 
-__device__ __forceinline__ void store_zero_row(void* o, int dtype, long long o_base) {
+__device__ __forceinline__ void store_zero_row(void* o, int dtype, long long o_base, bool sectors) {
   float z[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) z[i] = 0.f;
 #pragma unroll 1
   for (int c = 0; c < 8; ++c) {
     if (dtype == HYPERION_DTYPE_F32) {
-      store_row16<HYPERION_DTYPE_F32>(o, o_base + 16 * c, z);
+      store_row16<HYPERION_DTYPE_F32>(o, o_base + 16 * c, z, sectors);
     } else if (dtype == HYPERION_DTYPE_BF16) {
-      store_row16<HYPERION_DTYPE_BF16>(o, o_base + 16 * c, z);
+      store_row16<HYPERION_DTYPE_BF16>(o, o_base + 16 * c, z, sectors);
     } else {
-      store_row16<HYPERION_DTYPE_F16>(o, o_base + 16 * c, z);
+      store_row16<HYPERION_DTYPE_F16>(o, o_base + 16 * c, z, sectors);
     }
   }
 }
@@ -813,36 +826,36 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     const float m_safe = 128.f * cabs - 11.0f;
     const uint32_t tab_addr = smem_u32(&sm.ptab[0][0]);
     uint32_t uc = 0, kvit = 0, oc = 0;
-    for (;;) {
-      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) break;
-      int n_tiles, bh, row_end, item;
-      long long o_base;
-      bool row_ok;
-      {
-        const UnitInfo& u = sm.unit[uc & 1];
-        if (u.kind == 0) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.sched_empty[uc & 1]);
-          break;
-        }
-        const int r = t * kRows + row;
-        int q_idx = -1;
-        if (r >= u.seg_lo && r < u.seg_hi) {
-          const int qi = __ldg(&p.worklist[u.entry0 + r].x);
-          if (qi >= 0 && qi < p.seq_q) q_idx = qi;
-        }
-        row_ok = q_idx >= 0;
-        n_tiles = u.n_tiles;
-        bh = u.bh;
-        item = u.entry0 + r;
-        o_base = row_ok ? ((long long)u.bh * p.seq_q + q_idx) * 128 : 0;
-        row_end = row_ok ? (p.causal ? min(u.ctx, q_idx + 1) : u.ctx) : 0;
-      }
+    // The next unit is taken from its slot, and the global load of this row's q_idx
+    // issued, before the current unit's epilogue (the scheduler publishes units one
+    // ahead): the load's latency then hides behind the epilogue's stores.
+    UnitInfo nu;
+    int n_qi = -1;
+    auto fetch = [&]() -> bool {
+      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) return false;
+      nu = sm.unit[uc & 1];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.sched_empty[uc & 1]);
       ++uc;
+      const int r = t * kRows + row;
+      n_qi = (nu.kind != 0 && r >= nu.seg_lo && r < nu.seg_hi) ? __ldg(&p.worklist[nu.entry0 + r].x) : -1;
+      return true;
+    };
+    bool have = fetch();
+    while (have) {
+      const UnitInfo u = nu;
+      if (u.kind == 0) break;
+      const int r = t * kRows + row;
+      const int q_idx = (n_qi >= 0 && n_qi < p.seq_q) ? n_qi : -1;
+      const bool row_ok = q_idx >= 0;
+      const int n_tiles = u.n_tiles;
+      const int bh = u.bh;
+      const int item = u.entry0 + r;
+      const long long o_base = row_ok ? ((long long)u.bh * p.seq_q + q_idx) * 128 : 0;
+      const int row_end = row_ok ? (p.causal ? min(u.ctx, q_idx + 1) : u.ctx) : 0;
       if (n_tiles == 0) {
-        if (row_ok) store_zero_row(p.o, p.o_dtype, o_base);
+        if (row_ok) store_zero_row(p.o, p.o_dtype, o_base, p.o_align32);
+        have = fetch();
         continue;
       }
       float m = -INFINITY, l = 0.f;
@@ -931,6 +944,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         ++kvit;
       }
       if (ab) break;
+      have = fetch();
       // ---- epilogue: O row = acc * 256 * vscale / l
       if (!mbar_wait_warp(&sm.o_full[t], oc & 1, abort, p.err)) break;
       ++oc;
@@ -938,11 +952,11 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       const float vs = (p.v_scale_mode == 0) ? __ldg(p.v_scale) : __ldg(p.v_scale + (bh % p.v_scale_numel));
       const float scale = 256.f * vs * ((l > 1e-6f) ? 1.f / l : 1.f);
       if (p.o_dtype == HYPERION_DTYPE_BF16) {
-        store_o_row<HYPERION_DTYPE_BF16>(p.o, o_base, o_col, scale, row_ok);
+        store_o_row<HYPERION_DTYPE_BF16>(p.o, o_base, o_col, scale, row_ok, p.o_align32);
       } else if (p.o_dtype == HYPERION_DTYPE_F32) {
-        store_o_row<HYPERION_DTYPE_F32>(p.o, o_base, o_col, scale, row_ok);
+        store_o_row<HYPERION_DTYPE_F32>(p.o, o_base, o_col, scale, row_ok, p.o_align32);
       } else {
-        store_o_row<HYPERION_DTYPE_F16>(p.o, o_base, o_col, scale, row_ok);
+        store_o_row<HYPERION_DTYPE_F16>(p.o, o_base, o_col, scale, row_ok, p.o_align32);
       }
       tc::fence_before_sync();
       __syncwarp();
