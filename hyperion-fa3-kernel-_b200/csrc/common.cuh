@@ -205,6 +205,20 @@ __device__ __forceinline__ uint32_t fp8x2_even_to_f16x2_div256(uint32_t v) {
   return ((v << 7) & 0x3F803F80u) | ((v << 8) & 0x80008000u);
 }
 
+// Two FP8 e4m3 codes in the low 16 bits of `v` -> f16x2 (byte 0 in the low half)
+// by the hardware conversion: exact for every code except 0x7F and 0xFF, which it
+// turns into NaN where the reference decodes them to +-480.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2_hw(uint32_t v) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"((unsigned short)(v & 0xFFFFu)));
+  return r;
+}
+// Non-zero iff either half of the f16x2 `v` is a NaN (|bits| above 0x7C00): the
+// add carries into bit 15 of a half exactly then, and never across halves.
+__device__ __forceinline__ uint32_t f16x2_nan_bits(uint32_t v) {
+  return ((v & 0x7FFF7FFFu) + 0x03FF03FFu) & 0x80008000u;
+}
+
 // {a, b} -> f16x2 (a in the low half), round to nearest even.
 __device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
   uint32_t r;

@@ -15,7 +15,9 @@
 //   * consumers: 4 warps, each owning a quarter of every stage's keys with its own
 //     running (m, l, acc); the score is D - 2*popcount(q XOR k) (README.md:22),
 //     the softmax the reference's clamped online update (:544-572) applied per
-//     16-key group, and the FP8 decode the reference's rule (:122-141) as bit moves;
+//     16-key group, and the FP8 decode the hardware e4m3 conversion, which agrees
+//     with the reference's rule (:122-141) on every code but 0x7F / 0xFF; a group
+//     that holds one of those is redone with the rule itself, as bit moves;
 //   * the four per-warp states are merged through shared memory, then either
 //     finalised (:582-593) or written as a split-KV partial for the combine kernel.
 #pragma once
@@ -105,6 +107,15 @@ __global__ void __launch_bounds__(kThreads, 8) row_fwd_kernel(FwdParams p, int t
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+
+  // Zeros in the V stages, so that a slot no load ever fills decodes to 0 rather
+  // than to whatever an earlier kernel left in shared memory; the fence orders
+  // these stores before the bulk copies that later overwrite them.
+  {
+    uint4* v4 = reinterpret_cast<uint4*>(&sm.v[0][0]);
+    for (int i = threadIdx.x; i < kStages * Smem<D>::kVBytes / 16; i += kThreads) v4[i] = make_uint4(0u, 0u, 0u, 0u);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -296,17 +307,24 @@ __global__ void __launch_bounds__(kThreads, 8) row_fwd_kernel(FwdParams p, int t
 #pragma unroll
           for (int i = 0; i < DPL; ++i) acc[i] *= alpha;
           const uint8_t* vbase = &sm.v[s][(cw * kKeysPerWarp) * D];
-          if (p.v_scale_mode != 2) {
-            // Products on f16x2: w in [0, 1] and the decode / 256 in [-1.75, 1.75], so
-            // the sums over this warp's 16 keys stay below 28; they are added to the
-            // f32 accumulators once per stage.  A key that is absent has w = 0, and
-            // whatever bytes its V row holds decode to finite f16 values (the
-            // exponent field never reaches 31), so its products are 0.
+          bool exact = p.v_scale_mode == 2;
+          if (!exact) {
+            // Products on f16x2: w in [0, 1] and |V| <= 448, so the sums over this
+            // warp's 16 keys stay below 16 * 448 = 7168, inside the f16 range; they
+            // are added to the f32 accumulators once per stage.  A key that is
+            // absent has w = 0, so its products are 0 unless its bytes decode to NaN.
             if (lane < kKeysPerWarp) sm.wbuf[cw][lane] = pack_f16x2(w, w);
             __syncwarp();
-            uint32_t pe[NW], po[NW];
+            // The decode is the hardware e4m3 -> f16x2 conversion, 2 instructions
+            // per 4 bytes.  It reads codes 0x7F / 0xFF as NaN where the reference
+            // reads +-480, and a NaN poisons the sums of the lane that met it; the
+            // warp then redoes the group on the exact per-key path below.  The cache
+            // writer saturates to +-448 and never writes those codes, and the V
+            // slots a stage leaves unused hold zeros or earlier V rows, so the redo
+            // runs only for a cache written elsewhere that holds them.
+            uint32_t plo[NW], phi[NW];
 #pragma unroll
-            for (int i = 0; i < NW; ++i) pe[i] = po[i] = 0u;
+            for (int i = 0; i < NW; ++i) plo[i] = phi[i] = 0u;
 #pragma unroll
             for (int j4 = 0; j4 < kKeysPerWarp; j4 += 4) {
               const uint4 w4 = *reinterpret_cast<const uint4*>(&sm.wbuf[cw][j4]);
@@ -317,22 +335,32 @@ __global__ void __launch_bounds__(kThreads, 8) row_fwd_kernel(FwdParams p, int t
                 load_v_lane<D>(vbase + (j4 + u) * D, lane, vw);
 #pragma unroll
                 for (int i = 0; i < NW; ++i) {
-                  pe[i] = hfma2(wq[u], fp8x2_even_to_f16x2_div256(vw[i]), pe[i]);
-                  po[i] = hfma2(wq[u], fp8x2_odd_to_f16x2_div256(vw[i]), po[i]);
+                  plo[i] = hfma2(wq[u], e4m3x2_to_f16x2_hw(vw[i]), plo[i]);
+                  phi[i] = hfma2(wq[u], e4m3x2_to_f16x2_hw(vw[i] >> 16), phi[i]);
                 }
               }
             }
-            // pe[i] holds dims 4i and 4i+2 of this lane, po[i] dims 4i+1 and 4i+3.
+            uint32_t nan = 0u;
 #pragma unroll
-            for (int i = 0; i < NW; ++i) {
-              acc[4 * i + 0] = fmaf(f16_lo_to_f32(pe[i]), 256.f, acc[4 * i + 0]);
-              acc[4 * i + 1] = fmaf(f16_lo_to_f32(po[i]), 256.f, acc[4 * i + 1]);
-              acc[4 * i + 2] = fmaf(f16_hi_to_f32(pe[i]), 256.f, acc[4 * i + 2]);
-              acc[4 * i + 3] = fmaf(f16_hi_to_f32(po[i]), 256.f, acc[4 * i + 3]);
+            for (int i = 0; i < NW; ++i) nan |= f16x2_nan_bits(plo[i]) | f16x2_nan_bits(phi[i]);
+            if (!__any_sync(0xffffffffu, nan != 0u)) {
+              // plo[i] holds dims 4i and 4i+1 of this lane, phi[i] dims 4i+2 and 4i+3.
+#pragma unroll
+              for (int i = 0; i < NW; ++i) {
+                acc[4 * i + 0] += f16_lo_to_f32(plo[i]);
+                acc[4 * i + 1] += f16_hi_to_f32(plo[i]);
+                acc[4 * i + 2] += f16_lo_to_f32(phi[i]);
+                acc[4 * i + 3] += f16_hi_to_f32(phi[i]);
+              }
+            } else {
+              exact = true;
             }
-          } else {
-            // Per-slot V scale: w times the key's own scale, products in f32.
-            if (ok) {
+          }
+          if (exact) {
+            // Products in f32, one key at a time, with the exact bit-level decode:
+            // the path for a per-slot V scale (w times the key's own scale), and the
+            // redo of a group whose fast decode met a NaN code.
+            if (p.v_scale_mode == 2 && ok) {
               const int key = k0 + jl;
               const int page = key / p.block_size;
               const long long id = page_block_id(p, sl.bh, page);

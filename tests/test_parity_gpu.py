@@ -347,6 +347,43 @@ def test_row_path_large_scores_force_rescale(hyperion, oracle):
     check(oracle, wk, o)
 
 
+@pytest.mark.parametrize("path,D", [("row", 128), ("row", 256), ("tile", 128)])
+def test_every_fp8_code_in_the_cache(hyperion, oracle, path, D):
+    """V bytes drawn from all 256 codes, so 0x7F / 0xFF (+-480 in the reference's
+    decode, NaN to the hardware e4m3 conversion the row kernel's fast decode uses)
+    land in most groups: the row kernel must redo those groups exactly, and every
+    output must match the oracle."""
+    S_q = 3 if path == "row" else 150
+    wk = W.make_dense("codes", 1, 2, S_q, 1100, D=D, causal=(path == "tile"), scale_mode="head",
+                      o_dtype=torch.float32, seed=33)
+    gen = torch.Generator().manual_seed(34)
+    wk.v = torch.randint(0, 256, tuple(wk.v.shape), dtype=torch.uint8, generator=gen)
+    wk.v_scale = torch.tensor([0.004, 0.006], dtype=torch.float32)
+    assert int((wk.v == 0x7F).sum()) > 100 and int((wk.v == 0xFF).sum()) > 100
+    o, err, _ = run(hyperion, wk, path=path)
+    assert err == 0
+    assert np.isfinite(o).all()
+    check(oracle, wk, o)
+
+
+def test_row_path_sparse_nan_codes(hyperion, oracle):
+    """A cache from the quantiser with a few 0x7F / 0xFF codes planted in it: the
+    groups that hold one take the exact redo and the rest the fast decode, across
+    split-KV partials."""
+    wk = W.make_dense("nan_codes", 2, 2, 1, 5000, scale_mode="head", o_dtype=torch.float32, seed=35)
+    gen = torch.Generator().manual_seed(36)
+    v = wk.v.clone()
+    rows = torch.randint(0, v.shape[0], (40,), generator=gen)
+    cols = torch.randint(0, v.shape[1], (40,), generator=gen)
+    v[rows[:20], cols[:20]] = 0x7F
+    v[rows[20:], cols[20:]] = 0xFF
+    wk.v = v
+    o, err, _ = run(hyperion, wk, path="row", num_splits=4)
+    assert err == 0
+    assert np.isfinite(o).all()
+    check(oracle, wk, o)
+
+
 def test_tile_path_short_and_empty_contexts(hyperion, oracle):
     wk = W.make_dense("e", 1, 4, 256, 256, causal=False, o_dtype=torch.float32, seed=26)
     wk.ctx_lens[0] = 0
