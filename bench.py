@@ -1,6 +1,7 @@
 """Benchmark of the sign-bit / FP8 attention forward on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload prefill|decode|paged_decode|longctx|cpu_ref]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--workload prefill|decode|paged_decode|longctx|cpu_ref|decode_gqa|paged_decode_gqa]
                     [--impl ours|reference] [--path auto|row|tile] [--gather]
 
 For N > 1 launch with torchrun (one rank per GPU, NCCL):
@@ -132,11 +133,12 @@ def build_workload(name, rank, world, device):
         return wk, desc, "strong"
     wk = W.make_config(name, device=device, exact=False, seed=rank)
     c = W.CONFIGS[name]
-    if name == "paged_decode":
-        desc = (f"paged_decode B{c['B']} H{c['H']} D128 S_q=1, L~U[{c['lo']},{c['hi']}] seed 1, page {c['page']}, "
+    heads = f"H{c['H']}" + (f" over {c['Hkv']} KV heads" if "Hkv" in c else "")
+    if name.startswith("paged_decode"):
+        desc = (f"{name} B{c['B']} {heads} D128 S_q=1, L~U[{c['lo']},{c['hi']}] seed 1, page {c['page']}, "
                 "random page pool, per GPU")
     else:
-        desc = (f"{name} B{c['B']} H{c['H']} S_q={c['S_q']} S_kv={c['S_kv']} D128 "
+        desc = (f"{name} B{c['B']} {heads} S_q={c['S_q']} S_kv={c['S_kv']} D128 "
                 f"{'causal' if c['causal'] else 'non-causal'}, per GPU")
     return wk, desc, "weak"
 
@@ -144,14 +146,15 @@ def build_workload(name, rank, world, device):
 def call_forward(hyperion, wk, o, path="auto", **kw):
     hyperion.hyperion_apex_kernel(wk.worklist, wk.total_work, wk.q, None, wk.k, None, wk.v, wk.v_scale, wk.ctx_lens,
                                   wk.block_tables, o, wk.seq_q, wk.head_dim, wk.head_dim // 8, wk.block_size,
-                                  wk.num_blocks, wk.inv_sqrt_d, wk.causal, path=path, **kw)
+                                  wk.num_blocks, wk.inv_sqrt_d, wk.causal, path=path, kv_group=wk.kv_group, **kw)
 
 
 def roofline_numbers(wk, pairs, kernel_ms, pk):
     """Dominant kernel: algorithmic work per launch / average launch time."""
     if wk.seq_q == 1:
-        # decode: K (D/8 B) + V (D B) per pair, plus Q rows and O rows.
-        nbytes = pairs * wk.kv_bytes_per_pair() + wk.total_work * (wk.head_dim // 8) \
+        # decode: K (D/8 B) + V (D B) per distinct (KV row, key) pair, plus Q rows and
+        # O rows.  Without grouped-query heads every pair has its own KV row.
+        nbytes = wk.kv_keys() * wk.kv_bytes_per_pair() + wk.total_work * (wk.head_dim // 8) \
             + wk.total_work * wk.head_dim * torch.tensor([], dtype=wk.o_dtype).element_size()
         achieved = nbytes / (kernel_ms * 1e-3) / 1e9
         return {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
@@ -217,7 +220,8 @@ def _subset_rows(wk, rows):
     from hyperion_b200 import workloads as W
 
     cap = wk.num_blocks * wk.block_size
-    lens = [min(int(wk.ctx_lens[bh]), cap) for bh in rows]
+    g = wk.kv_group
+    lens = [min(int(wk.ctx_lens[bh // g]), cap) for bh in rows]
     Lmax = max(max(lens), 1)
     W_ = wk.head_dim // 32
     kk = torch.zeros(len(rows) * Lmax, W_, dtype=torch.int32, device=wk.k.device)
@@ -227,12 +231,13 @@ def _subset_rows(wk, rows):
     for i, (bh, L) in enumerate(zip(rows, lens)):
         t = torch.arange(L, device=wk.k.device)
         page = t // wk.block_size
-        ids = wk.block_tables[bh].to(torch.int64)[page] if wk.block_tables.numel() else bh * wk.num_blocks + page
+        kv = bh // g
+        ids = wk.block_tables[kv].to(torch.int64)[page] if wk.block_tables.numel() else kv * wk.num_blocks + page
         slots = ids * wk.block_size + t % wk.block_size
         kk[i * Lmax: i * Lmax + L] = wk.k[slots]
         vv[i * Lmax: i * Lmax + L] = wk.v[slots]
         qq.append(wk.q[bh * wk.seq_q:(bh + 1) * wk.seq_q])
-        sc.append(vs.reshape(-1)[0] if vs.numel() == 1 else vs[bh % vs.numel()])
+        sc.append(vs.reshape(-1)[0] if vs.numel() == 1 else vs[kv % vs.numel()])
     scale = torch.stack(sc).float()
     if scale.numel() == kk.shape[0]:  # keep the per-row scale unambiguous
         scale = torch.cat([scale, scale[:1]])
@@ -283,7 +288,7 @@ def run_e2e(hyperion, wk, o, args, barrier):
 
     Decode (one query row): the KV cache stays on the device, as the reference's
     engine keeps it (hyperion_fa3_production_final.py:1017-1032).  A step copies in
-    the new token's Q rows, K and V (bf16 [batch, heads, D]), positions and context
+    the new token's Q rows, K and V (bf16 [batch, KV heads, D]), positions and context
     lengths, writes K and V into the cache (kv_cache_write), runs the forward and
     copies O out.
     Prefill: a step copies in all of the forward's inputs and copies O out.  Steps
@@ -293,13 +298,13 @@ def run_e2e(hyperion, wk, o, args, barrier):
     dev = o.device
     main = torch.cuda.current_stream(dev)
     if wk.seq_q == 1:
-        B, H, D = wk.batch, wk.heads, wk.head_dim
-        ctx = wk.ctx_lens.view(B, H)[:, 0].to(torch.int32)
+        B, Hkv, D = wk.batch, wk.heads // wk.kv_group, wk.head_dim
+        ctx = wk.ctx_lens.view(B, Hkv)[:, 0].to(torch.int32)
         g = torch.Generator().manual_seed(5)
         host = {
             "q": wk.q.cpu().pin_memory(),
-            "k_new": torch.randn(B, H, D, generator=g).to(torch.bfloat16).pin_memory(),
-            "v_new": torch.randn(B, H, D, generator=g).to(torch.bfloat16).pin_memory(),
+            "k_new": torch.randn(B, Hkv, D, generator=g).to(torch.bfloat16).pin_memory(),
+            "v_new": torch.randn(B, Hkv, D, generator=g).to(torch.bfloat16).pin_memory(),
             "seq_ids": torch.arange(B, dtype=torch.int32).pin_memory(),
             "positions": (ctx - 1).clamp_min(0).cpu().pin_memory(),
             "ctx_lens": wk.ctx_lens.cpu().pin_memory(),
@@ -531,7 +536,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="prefill",
-                    choices=["prefill", "decode", "paged_decode", "longctx", "cpu_ref"])
+                    choices=["prefill", "decode", "paged_decode", "longctx", "cpu_ref", "decode_gqa",
+                             "paged_decode_gqa"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--path", default="auto", choices=["auto", "row", "tile"])
     ap.add_argument("--gather", action="store_true", help="also time the NCCL all-gather of O (N > 1)")

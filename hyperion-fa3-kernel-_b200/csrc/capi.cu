@@ -17,6 +17,7 @@
 
 #include "common.cuh"
 #include "row_kernel.cuh"
+#include "row_group_kernel.cuh"
 #include "tile_kernel.cuh"
 #include "kv_write.cuh"
 
@@ -40,6 +41,8 @@ struct DevInfo {
   int n_sm = 0;
   int row_ctas_128 = 1, row_ctas_256 = 1;
   int row_smem_128 = 0, row_smem_256 = 0;
+  int group_ctas_128 = 1, group_ctas_256 = 1;  // grouped-query row kernel
+  int group_smem_128 = 0, group_smem_256 = 0;
   int tile_ctas = 0, tile_smem = 0;
   bool tile_ok = false;
   std::string tile_why;  // why the tile kernel is unavailable ("" when it is)
@@ -60,6 +63,18 @@ int setup_row(int& ctas, int& smem) {
   return HYPERION_OK;
 }
 
+template <int D>
+int setup_group(int& ctas, int& smem) {
+  smem = (int)sizeof(hyp::row::GroupSmem<D>);
+  cudaError_t e =
+      cudaFuncSetAttribute(hyp::row::row_group_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(row group)");
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, hyp::row::row_group_kernel<D>, hyp::row::kThreads, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor(row group)");
+  if (ctas < 1) ctas = 1;
+  return HYPERION_OK;
+}
+
 int get_dev(const DevInfo** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -73,6 +88,10 @@ int get_dev(const DevInfo** out) {
     int rc = setup_row<128>(di.row_ctas_128, di.row_smem_128);
     if (rc) return rc;
     rc = setup_row<256>(di.row_ctas_256, di.row_smem_256);
+    if (rc) return rc;
+    rc = setup_group<128>(di.group_ctas_128, di.group_smem_128);
+    if (rc) return rc;
+    rc = setup_group<256>(di.group_ctas_256, di.group_smem_256);
     if (rc) return rc;
     const char* why = "";
     rc = hyp::tile::setup(di.tile_ctas, di.tile_smem, &why);
@@ -171,6 +190,10 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   if (ext->v_scale_numel < 1) return fail(HYPERION_ERR_INVALID_ARG, "V_scale is empty");
   if (ext->o_dtype != HYPERION_DTYPE_F16 && ext->o_dtype != HYPERION_DTYPE_BF16 && ext->o_dtype != HYPERION_DTYPE_F32)
     return fail(HYPERION_ERR_INVALID_ARG, "o_dtype is not F16, BF16 or F32");
+  if (opt && opt->kv_group < 0) return fail(HYPERION_ERR_INVALID_ARG, "kv_group < 0");
+  const int kv_group = (opt && opt->kv_group > 1) ? opt->kv_group : 1;
+  if ((long long)ext->n_bh * kv_group > 0x7fffffffLL)
+    return fail(HYPERION_ERR_INVALID_ARG, "n_bh * kv_group exceeds int32");
   const bool paged = ext->block_tables_numel != 0;
   if (paged) {
     if (block_tables == nullptr) return fail(HYPERION_ERR_INVALID_ARG, "block_tables is NULL but numel > 0");
@@ -212,7 +235,9 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   p.v_scale_numel = ext->v_scale_numel;
   p.v_scale_mode = (ext->v_scale_numel == 1) ? 0 : (ext->v_scale_numel == ext->pool_rows ? 2 : 1);
   p.ctx_lens = context_lens;
-  p.n_bh = ext->n_bh;
+  p.n_bh = ext->n_bh * kv_group;
+  p.kv_group = kv_group;
+  p.group_items = 1;
   p.block_tables = paged ? block_tables : nullptr;
   p.pool_rows = ext->pool_rows;
   p.pool_blocks = ext->pool_rows / block_size;
@@ -272,13 +297,31 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   p.n_split = ns;
   const long long units = (long long)total_work * ns;
   if (units > 0x7fffffffLL) return fail(HYPERION_ERR_UNSUPPORTED, "too many work units");
-  const int ctas = (head_dim == 256) ? di->row_ctas_256 : di->row_ctas_128;
-  const int smem = (head_dim == 256) ? di->row_smem_256 : di->row_smem_128;
-  const int grid = (int)std::min<long long>(units, (long long)di->n_sm * ctas);
-  if (head_dim == 256) {
-    hyp::row::row_fwd_kernel<256><<<grid, hyp::row::kThreads, smem, st>>>(p, (int)units);
+  int grid = 0;
+  if (kv_group > 1) {
+    // Grouped-query row kernel: a unit is up to 4 consecutive work items (the
+    // query heads of one KV head in a decode worklist) and one KV split.
+    p.group_items = std::min(kv_group, hyp::row::kGroupMax);
+    const long long chunks = ((long long)total_work + p.group_items - 1) / p.group_items;
+    const long long gunits = chunks * ns;
+    if (gunits > 0x7fffffffLL) return fail(HYPERION_ERR_UNSUPPORTED, "too many work units");
+    const int ctas = (head_dim == 256) ? di->group_ctas_256 : di->group_ctas_128;
+    const int smem = (head_dim == 256) ? di->group_smem_256 : di->group_smem_128;
+    grid = (int)std::min<long long>(gunits, (long long)di->n_sm * ctas);
+    if (head_dim == 256) {
+      hyp::row::row_group_kernel<256><<<grid, hyp::row::kThreads, smem, st>>>(p, (int)gunits);
+    } else {
+      hyp::row::row_group_kernel<128><<<grid, hyp::row::kThreads, smem, st>>>(p, (int)gunits);
+    }
   } else {
-    hyp::row::row_fwd_kernel<128><<<grid, hyp::row::kThreads, smem, st>>>(p, (int)units);
+    const int ctas = (head_dim == 256) ? di->row_ctas_256 : di->row_ctas_128;
+    const int smem = (head_dim == 256) ? di->row_smem_256 : di->row_smem_128;
+    grid = (int)std::min<long long>(units, (long long)di->n_sm * ctas);
+    if (head_dim == 256) {
+      hyp::row::row_fwd_kernel<256><<<grid, hyp::row::kThreads, smem, st>>>(p, (int)units);
+    } else {
+      hyp::row::row_fwd_kernel<128><<<grid, hyp::row::kThreads, smem, st>>>(p, (int)units);
+    }
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "row kernel launch");

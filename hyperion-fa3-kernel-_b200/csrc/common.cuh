@@ -36,10 +36,12 @@ struct FwdParams {
   const uint32_t* k;      // [pool_rows, W]
   const uint8_t* v;       // [pool_rows, D]
   const float* v_scale;
-  int v_scale_mode;       // 0 per tensor, 1 index bh % numel, 2 per slot
+  int v_scale_mode;       // 0 per tensor, 1 index kv_of(bh) % numel, 2 per slot
   long long v_scale_numel;
-  const int* ctx_lens;
-  int n_bh;
+  const int* ctx_lens;     // [n_bh / kv_group]: per KV (batch, head)
+  int n_bh;                // query (batch, head) rows: numel(ctx_lens) * kv_group
+  int kv_group;            // query heads per KV head (1: none); KV row of bh is bh / kv_group
+  int group_items;         // grouped row kernel: work items per unit (1..4)
   const int* block_tables;  // nullptr -> contiguous
   long long pool_rows;
   long long pool_blocks;    // pool_rows / block_size
@@ -57,6 +59,13 @@ struct FwdParams {
   int pages_all_valid;  // 1: every page id the kernels can read is inside the pool (host-checked)
   int o_align32;        // 1: O is 32-byte aligned, so a 16-value row piece is whole 32-byte sectors
 };
+
+// KV-side (batch, head) row of query row `bh`: grouped-query attention maps
+// kv_group consecutive query heads onto one KV head.  Context lengths, block-table
+// rows, the contiguous layout and a per-head V scale are all indexed by it.
+__device__ __forceinline__ int kv_of(const FwdParams& p, int bh) {
+  return p.kv_group == 1 ? bh : bh / p.kv_group;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -254,21 +263,26 @@ __device__ __forceinline__ int sign_score(const uint32_t (&q)[W], const uint32_t
 __device__ __forceinline__ float v_scale_for(const FwdParams& p, int bh, long long slot) {
   switch (p.v_scale_mode) {
     case 0: return __ldg(p.v_scale);
-    case 1: return __ldg(p.v_scale + (bh % p.v_scale_numel));
+    case 1: return __ldg(p.v_scale + (kv_of(p, bh) % p.v_scale_numel));
     default: return __ldg(p.v_scale + slot);
   }
 }
 
-// Page id of page `page` of (batch, head) row `bh`, or -1 when it lies outside the pool.
-__device__ __forceinline__ long long page_block_id(const FwdParams& p, int bh, int page) {
+// Page id of page `page` of KV row `kv`, or -1 when it lies outside the pool.
+__device__ __forceinline__ long long page_block_id_kv(const FwdParams& p, int kv, int page) {
   long long id;
   if (p.block_tables == nullptr) {
-    id = (long long)bh * p.num_blocks + page;
+    id = (long long)kv * p.num_blocks + page;
   } else {
-    id = __ldg(p.block_tables + (long long)bh * p.num_blocks + page);
+    id = __ldg(p.block_tables + (long long)kv * p.num_blocks + page);
   }
   if (id < 0 || id >= p.pool_blocks) return -1;
   return id;
+}
+
+// Page id of page `page` of query (batch, head) row `bh`, or -1 outside the pool.
+__device__ __forceinline__ long long page_block_id(const FwdParams& p, int bh, int page) {
+  return page_block_id_kv(p, kv_of(p, bh), page);
 }
 
 template <typename T>
@@ -308,7 +322,7 @@ __device__ __forceinline__ ItemInfo resolve_item(const FwdParams& p, int item) {
   r.valid = (r.bh >= 0 && r.bh < p.n_bh && r.q_idx >= 0 && r.q_idx < p.seq_q);
   r.kv_end = 0;
   if (!r.valid) return r;
-  int ctx = __ldg(p.ctx_lens + r.bh);
+  int ctx = __ldg(p.ctx_lens + kv_of(p, r.bh));
   const long long cap = (long long)p.num_blocks * p.block_size;
   if (ctx < 0) ctx = 0;
   if ((long long)ctx > cap) ctx = (int)cap;
@@ -325,7 +339,7 @@ __device__ __forceinline__ void check_item_errors(const FwdParams& p, int item) 
     raise_error(p.err, HYPERION_DEVERR_BAD_ITEM);
     return;
   }
-  const int ctx = __ldg(p.ctx_lens + bh);
+  const int ctx = __ldg(p.ctx_lens + kv_of(p, bh));
   if (ctx < 0) raise_error(p.err, HYPERION_DEVERR_NEG_CTX);
   if ((long long)ctx > (long long)p.num_blocks * p.block_size) raise_error(p.err, HYPERION_DEVERR_CTX_OVERFLOW);
 }

@@ -1,0 +1,500 @@
+// row_group_kernel.cuh -- the split-KV row kernel for grouped-query attention.
+//
+// With kv_group > 1, several query heads read the same KV head.  The reference
+// engine is configured that way (num_heads 32, num_kv_heads 8:
+// hyperion_fa3_production_final.py:852-853), but its kernel has no notion of it:
+// every (batch, head) row streams its own keys.  Here a unit is up to kGroupMax
+// consecutive work items and one KV split.  The producer cuts the unit into runs
+// of consecutive items on the same KV row and streams each run's keys once; every
+// consumer warp scores and accumulates all queries of the run against each stage.
+// HBM traffic per query falls by the run length.  The per-(query, key) arithmetic
+// is the row kernel's (popcount score, the reference's clamped online softmax per
+// 16-key group, f16x2 products of the hardware FP8 decode with the exact redo for
+// codes 0x7F / 0xFF), with the FP8 decode of a key shared by the run's queries.
+//
+// Each query keeps its own key range [0, kv_end), so a run may also hold rows of
+// one (batch, head) at different causal positions; the run streams the longest.
+#pragma once
+
+#include "row_kernel.cuh"
+
+namespace hyp {
+namespace row {
+
+constexpr int kGroupMax = 4;  // queries per run
+
+template <int W>
+struct RunSlot {
+  int unit;   // -1: no more work
+  int split;
+  int nq;     // queries of the run, 1..kGroupMax
+  int bh0;    // query row of the run's first item
+  int kv;     // the run's KV row
+  int k_lo;
+  int k_hi;
+  int item[kGroupMax];
+  int orow[kGroupMax];    // O row: bh * seq_q + q_idx
+  int kv_end[kGroupMax];  // the query attends keys [0, kv_end)
+  alignas(16) uint32_t q[kGroupMax][W];
+};
+
+template <int D>
+struct GroupSmem {
+  static constexpr int W = D / 32;
+  static constexpr int kKBytes = kKeysPerStage * W * 4;
+  static constexpr int kVBytes = kKeysPerStage * D;
+  alignas(128) uint8_t k[kStages][kKBytes];
+  alignas(128) uint8_t v[kStages][kVBytes];
+  StageHeader hdr[kStages];
+  RunSlot<W> slot[2];
+  float merge_m[kConsumerWarps];
+  float merge_l[kConsumerWarps];
+  float merge_acc[kConsumerWarps][D];
+  alignas(16) uint32_t wbuf[kConsumerWarps][kGroupMax][kKeysPerWarp];  // f16x2 {w, w} per query and key
+  alignas(8) uint64_t full[kStages];
+  alignas(8) uint64_t empty[kStages];
+  alignas(8) uint64_t run_full[2];
+  alignas(8) uint64_t run_empty[2];
+  int abort;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 4) row_group_kernel(FwdParams p, int total_units) {
+  constexpr int W = D / 32;
+  constexpr int DPL = D / 32;  // dims per lane
+  constexpr int NW = DPL / 4;  // 32-bit words of V bytes per lane and key
+  constexpr int G = kGroupMax;
+  static_assert(D == 128 || D == 256, "row kernel: head_dim 128 or 256");
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  GroupSmem<D>& sm = *reinterpret_cast<GroupSmem<D>*>(smem_raw);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Zeros in the V stages, so that a slot no load ever fills decodes to 0; the
+  // fence orders these stores before the bulk copies that overwrite them.
+  {
+    uint4* v4 = reinterpret_cast<uint4*>(&sm.v[0][0]);
+    for (int i = threadIdx.x; i < kStages * GroupSmem<D>::kVBytes / 16; i += kThreads)
+      v4[i] = make_uint4(0u, 0u, 0u, 0u);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], kConsumerWarps);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.run_full[s], 1);
+      mbar_init(&sm.run_empty[s], kConsumerWarps);
+    }
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  volatile int* abort = &sm.abort;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    const uint64_t pol = policy_evict_first();
+    uint32_t it = 0;  // stages armed
+    uint32_t rc = 0;  // run slots published
+    bool aborted = false;
+    for (;;) {
+      int t = 0;
+      if (lane == 0) t = (int)atomicAdd(&p.counters[0], 1u);
+      t = __shfl_sync(0xffffffffu, t, 0);
+      if (t >= total_units) {
+        const int us = rc & 1;
+        if (!mbar_wait_warp(&sm.run_empty[us], ((rc >> 1) & 1) ^ 1, abort, p.err)) break;
+        if (lane == 0) {
+          sm.slot[us].unit = -1;
+          mbar_arrive(&sm.run_full[us]);
+        }
+        ++rc;
+        break;
+      }
+      const int unit = t;
+      const int chunk = unit / p.n_split;
+      const int split = unit - chunk * p.n_split;
+      const int i0 = chunk * p.group_items;
+      const int n = min(p.group_items, p.total_work - i0);
+      // Lane j < n resolves item i0 + j.
+      ItemInfo inf;
+      inf.bh = 0;
+      inf.q_idx = 0;
+      inf.kv_end = 0;
+      inf.valid = false;
+      if (lane < n) {
+        inf = resolve_item(p, i0 + lane);
+        if (split == 0) check_item_errors(p, i0 + lane);
+      }
+      const int kvb = (lane < n && inf.valid) ? kv_of(p, inf.bh) : -1;
+      int r = 0;
+      while (r < n) {
+        const int kv_r = __shfl_sync(0xffffffffu, kvb, r);
+        if (kv_r < 0) {  // a bad item: flagged above, not written
+          ++r;
+          continue;
+        }
+        const unsigned diff = __ballot_sync(0xffffffffu, lane > r && lane < n && kvb != kv_r);
+        const int e = diff ? (__ffs(diff) - 1) : n;
+        const bool in_run = lane >= r && lane < e;
+        const int maxend = __reduce_max_sync(0xffffffffu, in_run ? inf.kv_end : 0);
+        int chunk_k = (maxend + p.n_split - 1) / p.n_split;
+        chunk_k = (chunk_k + 15) & ~15;
+        const int k_lo = min(split * chunk_k, maxend);
+        const int k_hi = min(k_lo + chunk_k, maxend);
+        const int bh_r = __shfl_sync(0xffffffffu, inf.bh, r);
+
+        const int us = rc & 1;
+        if (!mbar_wait_warp(&sm.run_empty[us], ((rc >> 1) & 1) ^ 1, abort, p.err)) {
+          aborted = true;
+          break;
+        }
+        RunSlot<W>& sl = sm.slot[us];
+        if (in_run) {
+          const int j = lane - r;
+          sl.item[j] = i0 + lane;
+          sl.orow[j] = inf.bh * p.seq_q + inf.q_idx;
+          sl.kv_end[j] = inf.kv_end;
+          const uint32_t* qrow = p.q + ((long long)inf.bh * p.seq_q + inf.q_idx) * W;
+#pragma unroll
+          for (int i = 0; i < W; ++i) sl.q[j][i] = __ldg(qrow + i);
+        }
+        if (lane == 0) {
+          sl.unit = unit;
+          sl.split = split;
+          sl.nq = e - r;
+          sl.bh0 = bh_r;
+          sl.kv = kv_r;
+          sl.k_lo = k_lo;
+          sl.k_hi = k_hi;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.run_full[us]);
+        ++rc;
+
+        for (int k0 = k_lo; k0 < k_hi; k0 += kKeysPerStage) {
+          const int s = it % kStages;
+          if (!mbar_wait_warp(&sm.empty[s], ((it / kStages) & 1) ^ 1, abort, p.err)) {
+            aborted = true;
+            break;
+          }
+          const int nk = min(kKeysPerStage, k_hi - k0);
+          const int bs = p.block_size;
+          const int p0 = k0 / bs;
+          const int np = (k0 + nk - 1) / bs - p0 + 1;
+          uint32_t bytes = 0;
+          unsigned long long mask = 0ull;
+          for (int i = lane; i < np; i += 32) {
+            const int page = p0 + i;
+            const int lo = max(k0, page * bs);
+            const int hi = min(k0 + nk, (page + 1) * bs);
+            const long long id = page_block_id_kv(p, kv_r, page);
+            if (id >= 0) {
+              bytes += (uint32_t)(hi - lo) * (uint32_t)(W * 4 + D);
+              const int a = lo - k0, b = hi - k0;
+              const unsigned long long bits = (b - a >= 64) ? ~0ull : ((1ull << (b - a)) - 1ull);
+              mask |= bits << a;
+            } else {
+              raise_error(p.err, HYPERION_DEVERR_BAD_BLOCK);
+            }
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
+            mask |= __shfl_xor_sync(0xffffffffu, mask, o);
+          }
+          if (lane == 0) {
+            sm.hdr[s].nkeys = nk;
+            sm.hdr[s].mask = mask;
+            if (bytes) {
+              mbar_arrive_expect_tx(&sm.full[s], bytes);
+            } else {
+              mbar_arrive(&sm.full[s]);
+            }
+          }
+          __syncwarp();
+          for (int i = lane; i < np; i += 32) {
+            const int page = p0 + i;
+            const int lo = max(k0, page * bs);
+            const int hi = min(k0 + nk, (page + 1) * bs);
+            const long long id = page_block_id_kv(p, kv_r, page);
+            if (id >= 0) {
+              const long long slot0 = id * bs + (lo - page * bs);
+              const uint32_t cnt = (uint32_t)(hi - lo);
+              bulk_g2s_stream(&sm.k[s][(lo - k0) * W * 4], p.k + slot0 * W, cnt * W * 4, &sm.full[s], pol);
+              bulk_g2s_stream(&sm.v[s][(lo - k0) * D], p.v + slot0 * D, cnt * D, &sm.full[s], pol);
+            }
+          }
+          ++it;
+        }
+        if (aborted) break;
+        r = e;
+      }
+      if (aborted) break;
+    }
+    if (*abort && lane == 0) {
+      // Let the copies of the last (up to kStages) armed stages land before exit.
+      for (uint32_t i = (it > (uint32_t)kStages ? it - kStages : 0u); i < it; ++i)
+        mbar_drain(&sm.full[i % kStages], (i / kStages) & 1);
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int cw = warp - 1;
+    uint32_t it = 0;
+    uint32_t rc = 0;
+    for (;;) {
+      const int us = rc & 1;
+      if (!mbar_wait_warp(&sm.run_full[us], (rc >> 1) & 1, abort, p.err)) break;
+      ++rc;
+      const RunSlot<W>& sl = sm.slot[us];
+      if (sl.unit < 0) break;
+      // The slot stays this run's until the warps release it after the merge.
+      const int nq = sl.nq;
+
+      float m[G], l[G], acc[G][DPL];
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        m[j] = -INFINITY;
+        l[j] = 0.f;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[j][i] = 0.f;
+      }
+
+      bool aborted = false;
+      for (int k0 = sl.k_lo; k0 < sl.k_hi; k0 += kKeysPerStage) {
+        const int s = it % kStages;
+        if (!mbar_wait_warp(&sm.full[s], (it / kStages) & 1, abort, p.err)) {
+          aborted = true;
+          break;
+        }
+        const int nk = sm.hdr[s].nkeys;
+        const unsigned long long mask = sm.hdr[s].mask;
+        const int jl = cw * kKeysPerWarp + (lane & 15);
+        const int key = k0 + jl;
+        const bool okk = (lane < 16) && (jl < nk) && ((mask >> jl) & 1ull);
+        uint32_t kr[W];
+#pragma unroll
+        for (int i = 0; i < W; ++i) kr[i] = 0u;
+        if (okk) {
+          const uint4* kp = reinterpret_cast<const uint4*>(&sm.k[s][jl * W * 4]);
+#pragma unroll
+          for (int i = 0; i < W / 4; ++i) {
+            const uint4 t4 = kp[i];
+            kr[4 * i + 0] = t4.x;
+            kr[4 * i + 1] = t4.y;
+            kr[4 * i + 2] = t4.z;
+            kr[4 * i + 3] = t4.w;
+          }
+        }
+        // Scores and the online-softmax step of every query of the run.
+        float w[G];
+        bool any_all = false;
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          w[j] = 0.f;
+          if (j < nq) {
+            const bool ok = okk && key < sl.kv_end[j];
+            int si = 0;
+            if (ok) {
+              const uint4* qp = reinterpret_cast<const uint4*>(&sl.q[j][0]);
+              int pc = 0;
+#pragma unroll
+              for (int i = 0; i < W / 4; ++i) {
+                const uint4 q4 = qp[i];
+                pc += __popc(q4.x ^ kr[4 * i + 0]) + __popc(q4.y ^ kr[4 * i + 1]) +
+                      __popc(q4.z ^ kr[4 * i + 2]) + __popc(q4.w ^ kr[4 * i + 3]);
+              }
+              si = D - 2 * pc;
+              if (p.debug_scores) p.debug_scores[(long long)sl.item[j] * p.debug_ld + key] = si;
+            }
+            int ext;
+            bool any;
+            if (p.inv_sqrt_d >= 0.f) {
+              ext = __reduce_max_sync(0xffffffffu, ok ? si : INT_MIN);
+              any = ext != INT_MIN;
+            } else {
+              ext = __reduce_min_sync(0xffffffffu, ok ? si : INT_MAX);
+              any = ext != INT_MAX;
+            }
+            if (any) {
+              const float mt = (float)ext * p.inv_sqrt_d;
+              const float sc = (float)si * p.inv_sqrt_d;
+              const float m_new = fmaxf(m[j], mt);
+              const float alpha = (m[j] == -INFINITY) ? 0.f : exp_clamped(m[j] - m_new);
+              w[j] = ok ? exp_clamped(sc - m_new) : 0.f;
+              l[j] = l[j] * alpha + w[j];
+#pragma unroll
+              for (int i = 0; i < DPL; ++i) acc[j][i] *= alpha;
+              m[j] = m_new;
+              any_all = true;
+            }
+          }
+        }
+        if (any_all) {
+          const uint8_t* vbase = &sm.v[s][(cw * kKeysPerWarp) * D];
+          bool exact = p.v_scale_mode == 2;
+          if (!exact) {
+            // f16x2 products of the hardware decode, shared by the run's queries;
+            // see row_fwd_kernel for the ranges and the NaN rule.
+            if (lane < kKeysPerWarp) {
+#pragma unroll
+              for (int j = 0; j < G; ++j) sm.wbuf[cw][j][lane] = pack_f16x2(w[j], w[j]);
+            }
+            __syncwarp();
+            uint32_t plo[G][NW], phi[G][NW];
+#pragma unroll
+            for (int j = 0; j < G; ++j) {
+#pragma unroll
+              for (int i = 0; i < NW; ++i) plo[j][i] = phi[j][i] = 0u;
+            }
+#pragma unroll
+            for (int j2 = 0; j2 < kKeysPerWarp; j2 += 2) {
+              uint2 wp[G];
+#pragma unroll
+              for (int j = 0; j < G; ++j) wp[j] = *reinterpret_cast<const uint2*>(&sm.wbuf[cw][j][j2]);
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                uint32_t vw[NW];
+                load_v_lane<D>(vbase + (j2 + u) * D, lane, vw);
+                uint32_t c0[NW], c1[NW];
+#pragma unroll
+                for (int i = 0; i < NW; ++i) {
+                  c0[i] = e4m3x2_to_f16x2_hw(vw[i]);
+                  c1[i] = e4m3x2_to_f16x2_hw(vw[i] >> 16);
+                }
+#pragma unroll
+                for (int j = 0; j < G; ++j) {
+                  if (j < nq) {
+                    const uint32_t wj = u ? wp[j].y : wp[j].x;
+#pragma unroll
+                    for (int i = 0; i < NW; ++i) {
+                      plo[j][i] = hfma2(wj, c0[i], plo[j][i]);
+                      phi[j][i] = hfma2(wj, c1[i], phi[j][i]);
+                    }
+                  }
+                }
+              }
+            }
+            uint32_t nan = 0u;
+#pragma unroll
+            for (int j = 0; j < G; ++j) {
+#pragma unroll
+              for (int i = 0; i < NW; ++i) nan |= f16x2_nan_bits(plo[j][i]) | f16x2_nan_bits(phi[j][i]);
+            }
+            if (!__any_sync(0xffffffffu, nan != 0u)) {
+              // plo[j][i] holds dims 4i and 4i+1 of this lane, phi[j][i] dims 4i+2 and 4i+3.
+#pragma unroll
+              for (int j = 0; j < G; ++j) {
+#pragma unroll
+                for (int i = 0; i < NW; ++i) {
+                  acc[j][4 * i + 0] += f16_lo_to_f32(plo[j][i]);
+                  acc[j][4 * i + 1] += f16_hi_to_f32(plo[j][i]);
+                  acc[j][4 * i + 2] += f16_lo_to_f32(phi[j][i]);
+                  acc[j][4 * i + 3] += f16_hi_to_f32(phi[j][i]);
+                }
+              }
+            } else {
+              exact = true;
+            }
+          }
+          if (exact) {
+            // Products in f32, one key at a time, with the exact bit-level decode:
+            // the path for a per-slot V scale, and the redo of a group whose fast
+            // decode met a NaN code.
+            float vsl = 1.f;
+            if (p.v_scale_mode == 2 && okk) {
+              const int page = key / p.block_size;
+              const long long id = page_block_id_kv(p, sl.kv, page);
+              vsl = __ldg(p.v_scale + id * p.block_size + (key - page * p.block_size));
+            }
+            float ws[G];
+#pragma unroll
+            for (int j = 0; j < G; ++j) ws[j] = w[j] * vsl * kTwoPow120;
+#pragma unroll 2
+            for (int jj = 0; jj < kKeysPerWarp; ++jj) {
+              float wk[G];
+              bool nz = false;
+#pragma unroll
+              for (int j = 0; j < G; ++j) {
+                wk[j] = __shfl_sync(0xffffffffu, ws[j], jj);
+                nz |= wk[j] != 0.f;
+              }
+              if (nz) {
+                uint32_t vw[NW];
+                load_v_lane<D>(vbase + jj * D, lane, vw);
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) {
+                  const float vd = fp8_bits_to_f32_scaled(vw[i >> 2] >> (8 * (i & 3)));
+#pragma unroll
+                  for (int j = 0; j < G; ++j) acc[j][i] = fmaf(wk[j], vd, acc[j][i]);
+                }
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.empty[s]);
+        ++it;
+      }
+      // Every consumer warp reaches the named barriers below for every query of the
+      // run, also when it gave up on a wait: the barriers have no timeout of their own.
+      const bool stop = aborted || (*abort != 0);
+      const float vs_run = (p.v_scale_mode == 2) ? 1.f : v_scale_for(p, sl.bh0, 0);
+
+      // ---- merge the four warps' (m, l, acc), one query at a time ----
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        if (j < nq) {
+          const float l_warp = warp_sum(l[j]);
+          if (lane == 0) {
+            sm.merge_m[cw] = m[j];
+            sm.merge_l[cw] = l_warp;
+          }
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) sm.merge_acc[cw][lane * DPL + i] = acc[j][i];
+          named_bar_sync(1, 32 * kConsumerWarps);
+          float M = -INFINITY;
+#pragma unroll
+          for (int w2 = 0; w2 < kConsumerWarps; ++w2) M = fmaxf(M, sm.merge_m[w2]);
+          float f[kConsumerWarps];
+          float L = 0.f;
+#pragma unroll
+          for (int w2 = 0; w2 < kConsumerWarps; ++w2) {
+            const float mw = sm.merge_m[w2];
+            f[w2] = (mw == -INFINITY) ? 0.f : exp_clamped(mw - M);
+            L += sm.merge_l[w2] * f[w2];
+          }
+          for (int d = cw * 32 + lane; d < D; d += 32 * kConsumerWarps) {
+            float a = 0.f;
+#pragma unroll
+            for (int w2 = 0; w2 < kConsumerWarps; ++w2) a += sm.merge_acc[w2][d] * f[w2];
+            a *= vs_run;
+            if (stop) continue;
+            if (p.n_split == 1) {
+              const float inv_l = (L > 1e-6f) ? 1.f / L : 1.f;
+              store_out(p.o, p.o_dtype, (long long)sl.orow[j] * D + d, a * inv_l);
+            } else {
+              float* part = p.partials + ((long long)sl.item[j] * p.n_split + sl.split) * (2 + D);
+              part[2 + d] = a;
+              if (d == 0) {
+                part[0] = M;
+                part[1] = L;
+              }
+            }
+          }
+          named_bar_sync(1, 32 * kConsumerWarps);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.run_empty[us]);
+      if (stop) break;
+    }
+  }
+}
+
+}  // namespace row
+}  // namespace hyp

@@ -48,12 +48,11 @@ struct StageHeader {
 struct UnitSlot {
   int unit;   // -1: no more work
   int item;
-  int bh;
-  int q_idx;
+  int orow;   // Q and O row: bh * seq_q + q_idx
   int k_lo;
   int k_hi;
   int valid;
-  int split;
+  int kv;     // KV row of bh
 };
 
 template <int D>
@@ -166,18 +165,18 @@ __global__ void __launch_bounds__(kThreads, 8) row_fwd_kernel(FwdParams p, int t
         UnitSlot& sl = sm.slot[us];
         sl.unit = unit;
         sl.item = item;
-        sl.bh = bh;
-        sl.q_idx = q_idx;
+        sl.orow = bh * p.seq_q + q_idx;
         sl.k_lo = k_lo;
         sl.k_hi = k_hi;
         sl.valid = valid ? 1 : 0;
-        sl.split = split;
+        sl.kv = kv_of(p, bh);
         mbar_arrive(&sm.unit_full[us]);
       }
       ++ucount;
       if (unit < 0) break;
 
       bool aborted = false;
+      const int kv = kv_of(p, bh);
       for (int k0 = k_lo; k0 < k_hi; k0 += kKeysPerStage) {
         const int s = it % kStages;
         if (!mbar_wait_warp(&sm.empty[s], ((it / kStages) & 1) ^ 1, abort, p.err)) {
@@ -194,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 8) row_fwd_kernel(FwdParams p, int t
           const int page = p0 + i;
           const int lo = max(k0, page * bs);
           const int hi = min(k0 + n, (page + 1) * bs);
-          const long long id = page_block_id(p, bh, page);
+          const long long id = page_block_id_kv(p, kv, page);
           if (id >= 0) {
             bytes += (uint32_t)(hi - lo) * (uint32_t)(W * 4 + D);
             const int a = lo - k0, b = hi - k0;
@@ -223,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 8) row_fwd_kernel(FwdParams p, int t
           const int page = p0 + i;
           const int lo = max(k0, page * bs);
           const int hi = min(k0 + n, (page + 1) * bs);
-          const long long id = page_block_id(p, bh, page);
+          const long long id = page_block_id_kv(p, kv, page);
           if (id >= 0) {
             const long long slot0 = id * bs + (lo - page * bs);
             const uint32_t cnt = (uint32_t)(hi - lo);
@@ -256,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 8) row_fwd_kernel(FwdParams p, int t
 
       uint32_t q[W];
       if (sl.valid) {
-        const uint32_t* qrow = p.q + ((long long)sl.bh * p.seq_q + sl.q_idx) * W;
+        const uint32_t* qrow = p.q + (long long)sl.orow * W;
 #pragma unroll
         for (int i = 0; i < W; ++i) q[i] = __ldg(qrow + i);
       } else {
@@ -363,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 8) row_fwd_kernel(FwdParams p, int t
             if (p.v_scale_mode == 2 && ok) {
               const int key = k0 + jl;
               const int page = key / p.block_size;
-              const long long id = page_block_id(p, sl.bh, page);
+              const long long id = page_block_id_kv(p, sl.kv, page);
               w *= __ldg(p.v_scale + id * p.block_size + (key - page * p.block_size));
             }
             w *= kTwoPow120;
@@ -410,7 +409,9 @@ __global__ void __launch_bounds__(kThreads, 8) row_fwd_kernel(FwdParams p, int t
         f[w2] = (mw == -INFINITY) ? 0.f : exp_clamped(mw - M);
         L += sm.merge_l[w2] * f[w2];
       }
-      const float vs_unit = (p.v_scale_mode == 2) ? 1.f : v_scale_for(p, sl.bh, 0);
+      const float vs_unit = (p.v_scale_mode == 0)   ? __ldg(p.v_scale)
+                            : (p.v_scale_mode == 1) ? __ldg(p.v_scale + (sl.kv % p.v_scale_numel))
+                                                    : 1.f;
       for (int d = cw * 32 + lane; d < D; d += 32 * kConsumerWarps) {
         float a = 0.f;
 #pragma unroll
@@ -420,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 8) row_fwd_kernel(FwdParams p, int t
         if (p.n_split == 1) {
           if (sl.valid) {
             const float inv_l = (L > 1e-6f) ? 1.f / L : 1.f;
-            store_out(p.o, p.o_dtype, ((long long)sl.bh * p.seq_q + sl.q_idx) * D + d, a * inv_l);
+            store_out(p.o, p.o_dtype, (long long)sl.orow * D + d, a * inv_l);
           }
         } else {
           float* part = p.partials + (long long)sl.unit * (2 + D);

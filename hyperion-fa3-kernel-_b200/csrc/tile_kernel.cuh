@@ -509,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           seg_lo = seg_hi;
           continue;
         }
-        int ctx = __ldg(p.ctx_lens + bh0);
+        int ctx = __ldg(p.ctx_lens + kv_of(p, bh0));
         if (ctx < 0) {
           if (lane == 0) raise_error(p.err, HYPERION_DEVERR_NEG_CTX);
           ctx = 0;
@@ -949,7 +949,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       if (!mbar_wait_warp(&sm.o_full[t], oc & 1, abort, p.err)) break;
       ++oc;
       tc::fence_after_sync();
-      const float vs = (p.v_scale_mode == 0) ? __ldg(p.v_scale) : __ldg(p.v_scale + (bh % p.v_scale_numel));
+      const float vs = (p.v_scale_mode == 0) ? __ldg(p.v_scale) : __ldg(p.v_scale + (kv_of(p, bh) % p.v_scale_numel));
       const float scale = 256.f * vs * ((l > 1e-6f) ? 1.f / l : 1.f);
       if (p.o_dtype == HYPERION_DTYPE_BF16) {
         store_o_row<HYPERION_DTYPE_BF16>(p.o, o_base, o_col, scale, row_ok, p.o_align32);

@@ -112,6 +112,7 @@ def hyperion_apex_kernel(
     path: str = "auto",
     num_splits: int = 0,
     debug_scores: Optional[torch.Tensor] = None,
+    kv_group: int = 1,
 ) -> None:
     """Enqueues the forward on the current CUDA stream of O's device (asynchronous).
 
@@ -119,6 +120,12 @@ def hyperion_apex_kernel(
     (hyperion_fa3_production_final.py:268-288).  `path`, `num_splits` and
     `debug_scores` (int32 [total_work, L]: receives head_dim - 2*popcount for
     every attended key) are extensions for tests and tuning.
+
+    `kv_group` (grouped-query attention): query heads per KV head.  Work items,
+    Q and O are indexed by the query row bh in [0, numel(context_lens) * kv_group);
+    context_lens, the block-table rows, the contiguous layout and a per-head
+    V_scale by the KV row bh // kv_group.  The row path streams each KV stage once
+    for up to 4 consecutive work items on the same KV row.
     """
     total_work = int(total_work)
     _check(O.is_cuda, "O must be a CUDA tensor")
@@ -137,7 +144,9 @@ def hyperion_apex_kernel(
     _check(O.is_contiguous(), "O must be contiguous")
     _check(head_dim in (128, 256), "head_dim must be 128 or 256")
     _check(k_packed_bytes == head_dim // 8, "k_packed_bytes must be head_dim // 8 (sign-bit K)")
-    n_bh = context_lens.numel()
+    _check(int(kv_group) >= 1, "kv_group must be >= 1")
+    n_kv = context_lens.numel()
+    n_bh = n_kv * int(kv_group)
     row_bytes = head_dim // 8
     _check(_nbytes(Q) >= n_bh * seq_q * row_bytes, "Q smaller than n_bh * seq_q rows of head_dim/8 bytes")
     _check(_nbytes(K_cache) % row_bytes == 0, "K_cache bytes must be a multiple of head_dim/8")
@@ -150,7 +159,7 @@ def hyperion_apex_kernel(
                "block_tables must be a contiguous CUDA tensor on O's device")
         _check(block_tables.dtype == torch.int32, "block_tables must be int32")
         bt_numel = block_tables.numel()
-        _check(bt_numel >= n_bh * num_blocks, "block_tables numel < n_bh * num_blocks")
+        _check(bt_numel >= n_kv * num_blocks, "block_tables numel < numel(context_lens) * num_blocks")
     if debug_scores is not None:
         _check(debug_scores.is_cuda and debug_scores.dtype == torch.int32 and debug_scores.dim() == 2
                and debug_scores.is_contiguous() and debug_scores.size(0) >= total_work,
@@ -164,11 +173,11 @@ def hyperion_apex_kernel(
             return int(x[i]) if len(x) > i else 0
         return int(x)
 
-    ext = _capi.Extents(n_bh, pool_rows, V_scale.numel(), bt_numel, _O_DTYPES[O.dtype],
+    ext = _capi.Extents(n_kv, pool_rows, V_scale.numel(), bt_numel, _O_DTYPES[O.dtype],
                         _hint(grid), _hint(block), _hint(shared))
     opt = _capi.Options(_PATHS[path], int(num_splits),
                         debug_scores.data_ptr() if debug_scores is not None else None,
-                        debug_scores.size(1) if debug_scores is not None else 0)
+                        debug_scores.size(1) if debug_scores is not None else 0, int(kv_group))
     with torch.cuda.device(dev):
         need = _capi.lib.hyperion_workspace_bytes(total_work, head_dim, block_size, num_blocks)
         _check(need > 0, f"hyperion_workspace_bytes failed: {_capi.last_error()}")

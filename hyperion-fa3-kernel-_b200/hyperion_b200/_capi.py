@@ -71,6 +71,7 @@ class Options(ctypes.Structure):
         ("num_splits", ctypes.c_int32),
         ("debug_scores", ctypes.c_void_p),
         ("debug_ld", ctypes.c_int64),
+        ("kv_group", ctypes.c_int32),
     ]
 
 

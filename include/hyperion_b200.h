@@ -81,7 +81,7 @@ extern "C" {
 #define HYPERION_PATH_TILE   2  /* 128-row tcgen05 tile kernel: head_dim 128, non per-slot V scale */
 
 typedef struct hyperion_extents {
-  int32_t n_bh;               /* numel of context_lens: number of (batch, head) rows */
+  int32_t n_bh;               /* numel of context_lens: number of (batch, head) rows (KV rows under kv_group) */
   int64_t pool_rows;          /* rows of K_cache and of V_cache */
   int64_t v_scale_numel;      /* numel of V_scale */
   int64_t block_tables_numel; /* numel of block_tables; 0 selects the contiguous layout */
@@ -98,6 +98,15 @@ typedef struct hyperion_options {
                             scores head_dim - 2*popcount for every key the item attends
                             (masked keys are left untouched); NULL in production */
   int64_t debug_ld;      /* row stride of debug_scores in elements */
+  int32_t kv_group;      /* grouped-query attention: query heads per KV head; 0 or 1 = none.
+                            Work items, Q and O stay indexed by the query row bh, in
+                            [0, n_bh * kv_group); context_lens, the block-table rows, the
+                            contiguous layout and a per-head V_scale are indexed by the KV
+                            row bh / kv_group, so ext->n_bh counts KV rows.  The row path
+                            then streams each KV stage once for up to 4 consecutive work
+                            items on the same KV row.  No counterpart in the reference,
+                            whose engine config has num_kv_heads (hyperion_fa3_production_final.py:853)
+                            but whose kernel reads one KV row per (batch, head). */
 } hyperion_options;
 
 /* Bytes of device workspace the forward needs for these sizes with the automatic

@@ -124,9 +124,50 @@ def forward_c(worklist, q, k, v, v_scale, ctx_lens, block_tables, seq_q, head_di
     return o, written[:tw].astype(bool), int(err.value), scores
 
 
+def expand_kv_group(ctx_lens, block_tables, v_scale, kv_group, num_blocks, pool_rows):
+    """Grouped-query attention restated as the plain problem: query row bh reads KV
+    row bh // kv_group, so the KV-side index arrays are repeated per query row.
+
+    Returns (context_lens, block_tables, v_scale) over n_kv * kv_group rows.  The
+    contiguous layout (empty table) becomes the explicit table kv * num_blocks + j.
+    A per-tensor or per-slot V scale is unchanged; a per-head / per-(batch, head)
+    one is indexed kv % numel, as the kernels do."""
+    g = int(kv_group)
+    ctx = _np(ctx_lens).astype(np.int32).reshape(-1)
+    n_kv = ctx.size
+    kv_of_bh = np.arange(n_kv * g, dtype=np.int64) // g
+    ctx_q = np.ascontiguousarray(ctx[kv_of_bh])
+    bt = _np(block_tables).astype(np.int32).reshape(-1) if block_tables is not None else np.zeros(0, np.int32)
+    if bt.size == 0:
+        table = kv_of_bh[:, None] * num_blocks + np.arange(num_blocks, dtype=np.int64)[None, :]
+        bt_q = np.ascontiguousarray(table.astype(np.int32))
+    else:
+        bt_q = np.ascontiguousarray(bt[: n_kv * num_blocks].reshape(n_kv, num_blocks)[kv_of_bh])
+    vs = _np(v_scale).astype(np.float32).reshape(-1)
+    if vs.size in (1, pool_rows):
+        vs_q = vs
+    else:
+        vs_q = np.ascontiguousarray(vs[kv_of_bh % vs.size])
+        if vs_q.size == pool_rows:
+            raise ValueError("expanded per-head V scale would read as per-slot: pick other sizes")
+    return ctx_q, bt_q, vs_q
+
+
+def _workload_arrays(wk):
+    """(v_scale, context_lens, block_tables) of a workload as the plain problem sees them."""
+    g = getattr(wk, "kv_group", 1)
+    if g == 1:
+        return wk.v_scale, wk.ctx_lens, wk.block_tables
+    W = wk.head_dim // 32
+    pool_rows = min(_np(wk.k).size // W, _np(wk.v).size // wk.head_dim)
+    ctx_q, bt_q, vs_q = expand_kv_group(wk.ctx_lens, wk.block_tables, wk.v_scale, g, wk.num_blocks, pool_rows)
+    return vs_q, ctx_q, bt_q
+
+
 def forward_workload_c(wk, nthreads=0, scores_ld=0, total_work=None):
     """forward_c over a hyperion_b200.workloads.Workload (moved to the CPU)."""
-    return forward_c(wk.worklist, wk.q, wk.k, wk.v, wk.v_scale, wk.ctx_lens, wk.block_tables, wk.seq_q,
+    vs, ctx, bt = _workload_arrays(wk)
+    return forward_c(wk.worklist, wk.q, wk.k, wk.v, vs, ctx, bt, wk.seq_q,
                      wk.head_dim, wk.block_size, wk.num_blocks, wk.inv_sqrt_d, wk.causal, scores_ld=scores_ld,
                      nthreads=nthreads, total_work=total_work)
 
@@ -202,7 +243,8 @@ def forward_numpy(worklist, q, k, v, v_scale, ctx_lens, block_tables, seq_q, hea
 
 
 def forward_workload_numpy(wk):
-    return forward_numpy(wk.worklist, wk.q, wk.k, wk.v, wk.v_scale, wk.ctx_lens, wk.block_tables, wk.seq_q,
+    vs, ctx, bt = _workload_arrays(wk)
+    return forward_numpy(wk.worklist, wk.q, wk.k, wk.v, vs, ctx, bt, wk.seq_q,
                          wk.head_dim, wk.block_size, wk.num_blocks, wk.inv_sqrt_d, wk.causal)
 
 

@@ -182,3 +182,53 @@ def test_error_flags_bad_block_bad_item_overflow_negative(oracle):
     wk2.ctx_lens[1] = 10**6
     _, _, err2, _ = oracle.forward_workload_c(wk2)
     assert err2 & oracle.ERR_NEG_CTX and err2 & oracle.ERR_CTX_OVERFLOW
+
+
+# ----------------------------------------------------------------------------- grouped-query attention
+@pytest.mark.parametrize("scale_mode", ["tensor", "head", "bh"])
+def test_gqa_oracle_equals_materialized_kv_copies(oracle, scale_mode):
+    """kv_group restated by index expansion must give, bit for bit, what the plain
+    problem gives when every query head holds its own copy of its KV head's rows."""
+    B, H, Hkv, S_q, S_kv, D = 2, 6, 2, 3, 90, 128
+    g = H // Hkv
+    wk = W.make_dense("gqa", B, H, S_q, S_kv, D=D, causal=True, scale_mode=scale_mode, o_dtype=torch.float32,
+                      seed=41, kv_heads=Hkv)
+    assert wk.kv_group == g and wk.n_bh == B * H and wk.n_kv_bh == B * Hkv
+    o_gqa, wr_gqa, err, _ = oracle.forward_workload_c(wk)
+    assert err == 0 and wr_gqa.all()
+
+    kv_of_bh = torch.arange(B * H) // g
+    k = wk.k.view(B * Hkv, S_kv, -1)[kv_of_bh].reshape(B * H * S_kv, -1)
+    v = wk.v.view(B * Hkv, S_kv, D)[kv_of_bh].reshape(B * H * S_kv, D)
+    vs = wk.v_scale
+    if scale_mode == "head":
+        vs = vs.repeat_interleave(g)  # per query head
+    elif scale_mode == "bh":
+        vs = vs[kv_of_bh]
+    ctx = wk.ctx_lens[kv_of_bh]
+    o_copy, wr_copy, err2, _ = oracle.forward_c(wk.worklist, wk.q, k, v, vs, ctx, None, S_q, D, S_kv, 1,
+                                                wk.inv_sqrt_d, True)
+    assert err2 == 0 and wr_copy.all()
+    assert np.array_equal(o_gqa, o_copy)
+
+
+def test_gqa_oracle_paged_c_vs_numpy(oracle):
+    wk = W.make_paged("gqa_p", 3, 8, [40, 333, 1000], page=16, seed=42, o_dtype=torch.float32, kv_heads=2)
+    assert wk.kv_group == 4 and wk.block_tables.shape[0] == 6
+    o_c, wr, err, _ = oracle.forward_workload_c(wk)
+    o_np, wr_np = oracle.forward_workload_numpy(wk)
+    assert err == 0 and wr.all() and wr_np.all()
+    assert np.abs(o_c - o_np).max() < 1e-5
+
+
+def test_gqa_expansion_of_index_arrays(oracle):
+    ctx = np.array([5, 7], np.int32)
+    bt = np.array([[3, 4], [8, 9]], np.int32)
+    ctx_q, bt_q, vs_q = oracle.expand_kv_group(ctx, bt, np.array([0.5, 0.25], np.float32), 3, 2, 1000)
+    assert ctx_q.tolist() == [5, 5, 5, 7, 7, 7]
+    assert bt_q.tolist() == [[3, 4]] * 3 + [[8, 9]] * 3
+    assert vs_q.tolist() == [0.5] * 3 + [0.25] * 3
+    # The contiguous layout becomes the explicit table kv * num_blocks + j.
+    _, bt_c, vs_t = oracle.expand_kv_group(ctx, None, np.array([2.0], np.float32), 2, 3, 1000)
+    assert bt_c.tolist() == [[0, 1, 2], [0, 1, 2], [3, 4, 5], [3, 4, 5]]
+    assert vs_t.tolist() == [2.0]
