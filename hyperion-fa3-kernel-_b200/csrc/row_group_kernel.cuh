@@ -290,27 +290,32 @@ __global__ void __launch_bounds__(kThreads, 4) row_group_kernel(FwdParams p, int
             kr[4 * i + 3] = t4.w;
           }
         }
-        // Scores and the online-softmax step of every query of the run.
+        // Scores and the online-softmax step of every query of the run.  A query
+        // past the run's end (j >= nq) scores nothing, keeps w = 0 and is never
+        // merged, so the product loop below needs no test on it.
         float w[G];
+        int si_all[G];
+        bool ok_all[G];
         bool any_all = false;
 #pragma unroll
         for (int j = 0; j < G; ++j) {
           w[j] = 0.f;
-          if (j < nq) {
-            const bool ok = okk && key < sl.kv_end[j];
-            int si = 0;
-            if (ok) {
-              const uint4* qp = reinterpret_cast<const uint4*>(&sl.q[j][0]);
-              int pc = 0;
+          const bool ok = okk && j < nq && key < sl.kv_end[j];
+          ok_all[j] = ok;
+          int si = 0;
+          if (ok) {
+            const uint4* qp = reinterpret_cast<const uint4*>(&sl.q[j][0]);
+            int pc = 0;
 #pragma unroll
-              for (int i = 0; i < W / 4; ++i) {
-                const uint4 q4 = qp[i];
-                pc += __popc(q4.x ^ kr[4 * i + 0]) + __popc(q4.y ^ kr[4 * i + 1]) +
-                      __popc(q4.z ^ kr[4 * i + 2]) + __popc(q4.w ^ kr[4 * i + 3]);
-              }
-              si = D - 2 * pc;
-              if (p.debug_scores) p.debug_scores[(long long)sl.item[j] * p.debug_ld + key] = si;
+            for (int i = 0; i < W / 4; ++i) {
+              const uint4 q4 = qp[i];
+              pc += __popc(q4.x ^ kr[4 * i + 0]) + __popc(q4.y ^ kr[4 * i + 1]) +
+                    __popc(q4.z ^ kr[4 * i + 2]) + __popc(q4.w ^ kr[4 * i + 3]);
             }
+            si = D - 2 * pc;
+          }
+          si_all[j] = si;
+          {
             int ext;
             bool any;
             if (p.inv_sqrt_d >= 0.f) {
@@ -333,6 +338,11 @@ __global__ void __launch_bounds__(kThreads, 4) row_group_kernel(FwdParams p, int
               any_all = true;
             }
           }
+        }
+        if (p.debug_scores) {
+#pragma unroll
+          for (int j = 0; j < G; ++j)
+            if (ok_all[j]) p.debug_scores[(long long)sl.item[j] * p.debug_ld + key] = si_all[j];
         }
         if (any_all) {
           const uint8_t* vbase = &sm.v[s][(cw * kKeysPerWarp) * D];
@@ -368,13 +378,11 @@ __global__ void __launch_bounds__(kThreads, 4) row_group_kernel(FwdParams p, int
                 }
 #pragma unroll
                 for (int j = 0; j < G; ++j) {
-                  if (j < nq) {
-                    const uint32_t wj = u ? wp[j].y : wp[j].x;
+                  const uint32_t wj = u ? wp[j].y : wp[j].x;
 #pragma unroll
-                    for (int i = 0; i < NW; ++i) {
-                      plo[j][i] = hfma2(wj, c0[i], plo[j][i]);
-                      phi[j][i] = hfma2(wj, c1[i], phi[j][i]);
-                    }
+                  for (int i = 0; i < NW; ++i) {
+                    plo[j][i] = hfma2(wj, c0[i], plo[j][i]);
+                    phi[j][i] = hfma2(wj, c1[i], phi[j][i]);
                   }
                 }
               }
