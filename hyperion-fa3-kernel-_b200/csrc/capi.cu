@@ -298,10 +298,12 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   const long long units = (long long)total_work * ns;
   if (units > 0x7fffffffLL) return fail(HYPERION_ERR_UNSUPPORTED, "too many work units");
   int grid = 0;
-  if (kv_group > 1) {
-    // Grouped-query row kernel: a unit is up to 4 consecutive work items (the
-    // query heads of one KV head in a decode worklist) and one KV split.
-    p.group_items = std::min(kv_group, hyp::row::kGroupMax);
+  if (kv_group > 1 || seq_q > 1) {
+    // Grouped row kernel: a unit is up to 4 consecutive work items and one KV
+    // split, and a run of them on one KV row streams its keys once: the query
+    // heads of one KV head (grouped-query attention), or neighbouring query rows
+    // of one (batch, head) in a prefill worklist.
+    p.group_items = (kv_group > 1) ? std::min(kv_group, hyp::row::kGroupMax) : hyp::row::kGroupMax;
     const long long chunks = ((long long)total_work + p.group_items - 1) / p.group_items;
     const long long gunits = chunks * ns;
     if (gunits > 0x7fffffffLL) return fail(HYPERION_ERR_UNSUPPORTED, "too many work units");

@@ -16,12 +16,20 @@
 // one (batch, head) at different causal positions; the run streams the longest.
 #pragma once
 
+#include <type_traits>
+
 #include "row_kernel.cuh"
 
 namespace hyp {
 namespace row {
 
 constexpr int kGroupMax = 4;  // queries per run
+// KV ring depth: the kernel holds 96 registers a thread, so 4 CTAs share an SM
+// (the row kernel fits 8), and for head_dim 128 a ring of 4 stages keeps as many
+// stages in flight; for head_dim 256 four CTAs of 4 stages would not fit in
+// shared memory, and the ring stays at 2.
+template <int D>
+constexpr int group_stages() { return D == 128 ? 4 : 2; }
 
 template <int W>
 struct RunSlot {
@@ -43,16 +51,17 @@ struct GroupSmem {
   static constexpr int W = D / 32;
   static constexpr int kKBytes = kKeysPerStage * W * 4;
   static constexpr int kVBytes = kKeysPerStage * D;
-  alignas(128) uint8_t k[kStages][kKBytes];
-  alignas(128) uint8_t v[kStages][kVBytes];
-  StageHeader hdr[kStages];
+  static constexpr int NS = group_stages<D>();
+  alignas(128) uint8_t k[NS][kKBytes];
+  alignas(128) uint8_t v[NS][kVBytes];
+  StageHeader hdr[NS];
   RunSlot<W> slot[2];
   float merge_m[kConsumerWarps];
   float merge_l[kConsumerWarps];
   float merge_acc[kConsumerWarps][D];
   alignas(16) uint32_t wbuf[kConsumerWarps][kGroupMax][kKeysPerWarp];  // f16x2 {w, w} per query and key
-  alignas(8) uint64_t full[kStages];
-  alignas(8) uint64_t empty[kStages];
+  alignas(8) uint64_t full[NS];
+  alignas(8) uint64_t empty[NS];
   alignas(8) uint64_t run_full[2];
   alignas(8) uint64_t run_empty[2];
   int abort;
@@ -64,6 +73,7 @@ __global__ void __launch_bounds__(kThreads, 4) row_group_kernel(FwdParams p, int
   constexpr int DPL = D / 32;  // dims per lane
   constexpr int NW = DPL / 4;  // 32-bit words of V bytes per lane and key
   constexpr int G = kGroupMax;
+  constexpr int kGStages = GroupSmem<D>::NS;
   static_assert(D == 128 || D == 256, "row kernel: head_dim 128 or 256");
   extern __shared__ __align__(128) uint8_t smem_raw[];
   GroupSmem<D>& sm = *reinterpret_cast<GroupSmem<D>*>(smem_raw);
@@ -75,12 +85,12 @@ __global__ void __launch_bounds__(kThreads, 4) row_group_kernel(FwdParams p, int
   // fence orders these stores before the bulk copies that overwrite them.
   {
     uint4* v4 = reinterpret_cast<uint4*>(&sm.v[0][0]);
-    for (int i = threadIdx.x; i < kStages * GroupSmem<D>::kVBytes / 16; i += kThreads)
+    for (int i = threadIdx.x; i < kGStages * GroupSmem<D>::kVBytes / 16; i += kThreads)
       v4[i] = make_uint4(0u, 0u, 0u, 0u);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kGStages; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], kConsumerWarps);
     }
@@ -177,8 +187,8 @@ __global__ void __launch_bounds__(kThreads, 4) row_group_kernel(FwdParams p, int
         ++rc;
 
         for (int k0 = k_lo; k0 < k_hi; k0 += kKeysPerStage) {
-          const int s = it % kStages;
-          if (!mbar_wait_warp(&sm.empty[s], ((it / kStages) & 1) ^ 1, abort, p.err)) {
+          const int s = it % kGStages;
+          if (!mbar_wait_warp(&sm.empty[s], ((it / kGStages) & 1) ^ 1, abort, p.err)) {
             aborted = true;
             break;
           }
@@ -237,9 +247,9 @@ __global__ void __launch_bounds__(kThreads, 4) row_group_kernel(FwdParams p, int
       if (aborted) break;
     }
     if (*abort && lane == 0) {
-      // Let the copies of the last (up to kStages) armed stages land before exit.
-      for (uint32_t i = (it > (uint32_t)kStages ? it - kStages : 0u); i < it; ++i)
-        mbar_drain(&sm.full[i % kStages], (i / kStages) & 1);
+      // Let the copies of the last (up to kGStages) armed stages land before exit.
+      for (uint32_t i = (it > (uint32_t)kGStages ? it - kGStages : 0u); i < it; ++i)
+        mbar_drain(&sm.full[i % kGStages], (i / kGStages) & 1);
     }
   } else {
     // ------------------------------------------------------------ consumers
@@ -266,56 +276,60 @@ __global__ void __launch_bounds__(kThreads, 4) row_group_kernel(FwdParams p, int
 
       bool aborted = false;
       for (int k0 = sl.k_lo; k0 < sl.k_hi; k0 += kKeysPerStage) {
-        const int s = it % kStages;
-        if (!mbar_wait_warp(&sm.full[s], (it / kStages) & 1, abort, p.err)) {
+        const int s = it % kGStages;
+        if (!mbar_wait_warp(&sm.full[s], (it / kGStages) & 1, abort, p.err)) {
           aborted = true;
           break;
         }
-        const int nk = sm.hdr[s].nkeys;
-        const unsigned long long mask = sm.hdr[s].mask;
-        const int jl = cw * kKeysPerWarp + (lane & 15);
-        const int key = k0 + jl;
-        const bool okk = (lane < 16) && (jl < nk) && ((mask >> jl) & 1ull);
-        uint32_t kr[W];
+        // One stage for a run of NQ queries: NQ = 1 and NQ = G are compiled with
+        // constant trip counts, NQ = 0 takes the run's length at run time.
+        auto stage = [&](auto nqc) {
+          constexpr int NQ = decltype(nqc)::value;
+          constexpr int JN = (NQ == 0) ? G : NQ;  // query slots the loops visit
+          const int nk = sm.hdr[s].nkeys;
+          const unsigned long long mask = sm.hdr[s].mask;
+          const int jl = cw * kKeysPerWarp + (lane & 15);
+          const int key = k0 + jl;
+          const bool okk = (lane < 16) && (jl < nk) && ((mask >> jl) & 1ull);
+          uint32_t kr[W];
 #pragma unroll
-        for (int i = 0; i < W; ++i) kr[i] = 0u;
-        if (okk) {
-          const uint4* kp = reinterpret_cast<const uint4*>(&sm.k[s][jl * W * 4]);
-#pragma unroll
-          for (int i = 0; i < W / 4; ++i) {
-            const uint4 t4 = kp[i];
-            kr[4 * i + 0] = t4.x;
-            kr[4 * i + 1] = t4.y;
-            kr[4 * i + 2] = t4.z;
-            kr[4 * i + 3] = t4.w;
-          }
-        }
-        // Scores and the online-softmax step of every query of the run.  A query
-        // past the run's end (j >= nq) scores nothing, keeps w = 0 and is never
-        // merged, so the product loop below needs no test on it.
-        float w[G];
-        int si_all[G];
-        bool ok_all[G];
-        bool any_all = false;
-#pragma unroll
-        for (int j = 0; j < G; ++j) {
-          w[j] = 0.f;
-          const bool ok = okk && j < nq && key < sl.kv_end[j];
-          ok_all[j] = ok;
-          int si = 0;
-          if (ok) {
-            const uint4* qp = reinterpret_cast<const uint4*>(&sl.q[j][0]);
-            int pc = 0;
+          for (int i = 0; i < W; ++i) kr[i] = 0u;
+          if (okk) {
+            const uint4* kp = reinterpret_cast<const uint4*>(&sm.k[s][jl * W * 4]);
 #pragma unroll
             for (int i = 0; i < W / 4; ++i) {
-              const uint4 q4 = qp[i];
-              pc += __popc(q4.x ^ kr[4 * i + 0]) + __popc(q4.y ^ kr[4 * i + 1]) +
-                    __popc(q4.z ^ kr[4 * i + 2]) + __popc(q4.w ^ kr[4 * i + 3]);
+              const uint4 t4 = kp[i];
+              kr[4 * i + 0] = t4.x;
+              kr[4 * i + 1] = t4.y;
+              kr[4 * i + 2] = t4.z;
+              kr[4 * i + 3] = t4.w;
             }
-            si = D - 2 * pc;
           }
-          si_all[j] = si;
-          {
+          // Scores and the online-softmax step of every query of the run.  A query
+          // slot past the run's end (j >= nq) scores nothing, keeps w = 0 and is
+          // never merged, so the product loop below needs no test on it.
+          float w[JN];
+          int si_all[JN];
+          bool ok_all[JN];
+          bool any_all = false;
+#pragma unroll
+          for (int j = 0; j < JN; ++j) {
+            w[j] = 0.f;
+            const bool ok = okk && (NQ != 0 || j < nq) && key < sl.kv_end[j];
+            ok_all[j] = ok;
+            int si = 0;
+            if (ok) {
+              const uint4* qp = reinterpret_cast<const uint4*>(&sl.q[j][0]);
+              int pc = 0;
+#pragma unroll
+              for (int i = 0; i < W / 4; ++i) {
+                const uint4 q4 = qp[i];
+                pc += __popc(q4.x ^ kr[4 * i + 0]) + __popc(q4.y ^ kr[4 * i + 1]) +
+                      __popc(q4.z ^ kr[4 * i + 2]) + __popc(q4.w ^ kr[4 * i + 3]);
+              }
+              si = D - 2 * pc;
+            }
+            si_all[j] = si;
             int ext;
             bool any;
             if (p.inv_sqrt_d >= 0.f) {
@@ -338,13 +352,12 @@ __global__ void __launch_bounds__(kThreads, 4) row_group_kernel(FwdParams p, int
               any_all = true;
             }
           }
-        }
-        if (p.debug_scores) {
+          if (p.debug_scores) {
 #pragma unroll
-          for (int j = 0; j < G; ++j)
-            if (ok_all[j]) p.debug_scores[(long long)sl.item[j] * p.debug_ld + key] = si_all[j];
-        }
-        if (any_all) {
+            for (int j = 0; j < JN; ++j)
+              if (ok_all[j]) p.debug_scores[(long long)sl.item[j] * p.debug_ld + key] = si_all[j];
+          }
+          if (!any_all) return;
           const uint8_t* vbase = &sm.v[s][(cw * kKeysPerWarp) * D];
           bool exact = p.v_scale_mode == 2;
           if (!exact) {
@@ -352,20 +365,20 @@ __global__ void __launch_bounds__(kThreads, 4) row_group_kernel(FwdParams p, int
             // see row_fwd_kernel for the ranges and the NaN rule.
             if (lane < kKeysPerWarp) {
 #pragma unroll
-              for (int j = 0; j < G; ++j) sm.wbuf[cw][j][lane] = pack_f16x2(w[j], w[j]);
+              for (int j = 0; j < JN; ++j) sm.wbuf[cw][j][lane] = pack_f16x2(w[j], w[j]);
             }
             __syncwarp();
-            uint32_t plo[G][NW], phi[G][NW];
+            uint32_t plo[JN][NW], phi[JN][NW];
 #pragma unroll
-            for (int j = 0; j < G; ++j) {
+            for (int j = 0; j < JN; ++j) {
 #pragma unroll
               for (int i = 0; i < NW; ++i) plo[j][i] = phi[j][i] = 0u;
             }
 #pragma unroll
             for (int j2 = 0; j2 < kKeysPerWarp; j2 += 2) {
-              uint2 wp[G];
+              uint2 wp[JN];
 #pragma unroll
-              for (int j = 0; j < G; ++j) wp[j] = *reinterpret_cast<const uint2*>(&sm.wbuf[cw][j][j2]);
+              for (int j = 0; j < JN; ++j) wp[j] = *reinterpret_cast<const uint2*>(&sm.wbuf[cw][j][j2]);
 #pragma unroll
               for (int u = 0; u < 2; ++u) {
                 uint32_t vw[NW];
@@ -377,26 +390,28 @@ __global__ void __launch_bounds__(kThreads, 4) row_group_kernel(FwdParams p, int
                   c1[i] = e4m3x2_to_f16x2_hw(vw[i] >> 16);
                 }
 #pragma unroll
-                for (int j = 0; j < G; ++j) {
-                  const uint32_t wj = u ? wp[j].y : wp[j].x;
+                for (int j = 0; j < JN; ++j) {
+                  if (NQ != 0 || j < nq) {
+                    const uint32_t wj = u ? wp[j].y : wp[j].x;
 #pragma unroll
-                  for (int i = 0; i < NW; ++i) {
-                    plo[j][i] = hfma2(wj, c0[i], plo[j][i]);
-                    phi[j][i] = hfma2(wj, c1[i], phi[j][i]);
+                    for (int i = 0; i < NW; ++i) {
+                      plo[j][i] = hfma2(wj, c0[i], plo[j][i]);
+                      phi[j][i] = hfma2(wj, c1[i], phi[j][i]);
+                    }
                   }
                 }
               }
             }
             uint32_t nan = 0u;
 #pragma unroll
-            for (int j = 0; j < G; ++j) {
+            for (int j = 0; j < JN; ++j) {
 #pragma unroll
               for (int i = 0; i < NW; ++i) nan |= f16x2_nan_bits(plo[j][i]) | f16x2_nan_bits(phi[j][i]);
             }
             if (!__any_sync(0xffffffffu, nan != 0u)) {
               // plo[j][i] holds dims 4i and 4i+1 of this lane, phi[j][i] dims 4i+2 and 4i+3.
 #pragma unroll
-              for (int j = 0; j < G; ++j) {
+              for (int j = 0; j < JN; ++j) {
 #pragma unroll
                 for (int i = 0; i < NW; ++i) {
                   acc[j][4 * i + 0] += f16_lo_to_f32(plo[j][i]);
@@ -419,15 +434,15 @@ __global__ void __launch_bounds__(kThreads, 4) row_group_kernel(FwdParams p, int
               const long long id = page_block_id_kv(p, sl.kv, page);
               vsl = __ldg(p.v_scale + id * p.block_size + (key - page * p.block_size));
             }
-            float ws[G];
+            float ws[JN];
 #pragma unroll
-            for (int j = 0; j < G; ++j) ws[j] = w[j] * vsl * kTwoPow120;
+            for (int j = 0; j < JN; ++j) ws[j] = w[j] * vsl * kTwoPow120;
 #pragma unroll 2
             for (int jj = 0; jj < kKeysPerWarp; ++jj) {
-              float wk[G];
+              float wk[JN];
               bool nz = false;
 #pragma unroll
-              for (int j = 0; j < G; ++j) {
+              for (int j = 0; j < JN; ++j) {
                 wk[j] = __shfl_sync(0xffffffffu, ws[j], jj);
                 nz |= wk[j] != 0.f;
               }
@@ -438,11 +453,18 @@ __global__ void __launch_bounds__(kThreads, 4) row_group_kernel(FwdParams p, int
                 for (int i = 0; i < DPL; ++i) {
                   const float vd = fp8_bits_to_f32_scaled(vw[i >> 2] >> (8 * (i & 3)));
 #pragma unroll
-                  for (int j = 0; j < G; ++j) acc[j][i] = fmaf(wk[j], vd, acc[j][i]);
+                  for (int j = 0; j < JN; ++j) acc[j][i] = fmaf(wk[j], vd, acc[j][i]);
                 }
               }
             }
           }
+        };
+        if (nq == G) {
+          stage(std::integral_constant<int, G>{});
+        } else if (nq == 1) {
+          stage(std::integral_constant<int, 1>{});
+        } else {
+          stage(std::integral_constant<int, 0>{});
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.empty[s]);
