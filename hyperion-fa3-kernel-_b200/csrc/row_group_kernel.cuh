@@ -24,12 +24,10 @@ namespace hyp {
 namespace row {
 
 constexpr int kGroupMax = 4;  // queries per run
-// KV ring depth: the kernel holds 96 registers a thread, so 4 CTAs share an SM
-// (the row kernel fits 8), and for head_dim 128 a ring of 4 stages keeps as many
-// stages in flight; for head_dim 256 four CTAs of 4 stages would not fit in
-// shared memory, and the ring stays at 2.
+// KV ring depth: 3 stages for head_dim 128 (6 CTAs of them fit an SM's shared
+// memory), 2 for head_dim 256 (4 CTAs).
 template <int D>
-constexpr int group_stages() { return D == 128 ? 4 : 2; }
+constexpr int group_stages() { return D == 128 ? 3 : 2; }
 
 template <int W>
 struct RunSlot {
@@ -67,8 +65,16 @@ struct GroupSmem {
   int abort;
 };
 
+// Resident CTAs per SM the register budget is set for.  The kernel is bound by
+// instruction issue and latency rather than HBM, so more resident warps pay: for
+// head_dim 128, 6 CTAs (64 registers, a few bytes spilled) ran decode with 32 query
+// heads over 8 KV heads in 0.245 ms where 5 CTAs (72, none) took 0.254 ms and 4
+// CTAs 0.258 ms; head_dim 256 needs 96 registers (4 CTAs).
 template <int D>
-__global__ void __launch_bounds__(kThreads, 4) row_group_kernel(FwdParams p, int total_units) {
+constexpr int group_ctas() { return D == 128 ? 6 : 4; }
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, group_ctas<D>()) row_group_kernel(FwdParams p, int total_units) {
   constexpr int W = D / 32;
   constexpr int DPL = D / 32;  // dims per lane
   constexpr int NW = DPL / 4;  // 32-bit words of V bytes per lane and key

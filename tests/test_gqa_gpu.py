@@ -66,9 +66,10 @@ def test_gqa_paged_decode(hyperion, oracle, num_splits):
 
 
 def test_gqa_equals_block_tables_repeated_per_query_head(hyperion, oracle):
-    """The same problem given to the plain kernel, every query head's block-table row
-    pointing at its KV head's pages, reads the same keys in the same groups: the two
-    outputs agree to rounding."""
+    """The same problem given to the ungrouped kernel, every query head's block-table
+    row pointing at its KV head's pages.  Both meet the bar against the oracle; they
+    differ only by rounding (the grouped kernel accumulates f16 products on the tensor
+    cores in f32, the ungrouped one sums 16-key groups of f16x2 products first)."""
     wk = W.make_paged("gqa_eq", 3, 8, [100, 999, 3000], page=16, seed=53, o_dtype=torch.float32, kv_heads=2)
     o_g, err, _, _ = run(hyperion, wk, path="row", num_splits=2)
     assert err == 0
@@ -78,7 +79,9 @@ def test_gqa_equals_block_tables_repeated_per_query_head(hyperion, oracle):
                           ctx=wk.ctx_lens[kv_of_bh].contiguous(),
                           v_scale=wk.v_scale.repeat_interleave(wk.kv_group))
     assert err2 == 0
-    assert np.abs(o_g - o_p).max() <= 1e-6
+    check(oracle, wk, o_g)
+    check(oracle, wk, o_p)
+    assert np.abs(o_g - o_p).max() <= 2e-3
 
 
 @pytest.mark.parametrize("path", ["row", "tile"])
