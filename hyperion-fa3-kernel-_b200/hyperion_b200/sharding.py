@@ -8,7 +8,9 @@ collective is an optional gather of O for a caller that wants the whole output o
 every rank; a tensor-parallel consumer keeps its head block instead.
 
 Heads are split in contiguous blocks (the first H % world ranks take one extra), so
-a rank's rows are the same head block in every batch entry.
+a rank's rows are the same head block in every batch entry.  With grouped-query
+heads (kv_group > 1) the KV heads are split instead and a rank owns the query heads
+of its KV heads, so no KV head is read on two ranks.
 """
 from __future__ import annotations
 
@@ -19,13 +21,17 @@ import torch
 from .workloads import Workload, dense_worklist
 
 
-def head_range(n_heads: int, world: int, rank: int) -> range:
-    """Contiguous block of heads owned by `rank`; blocks differ in size by at most one."""
+def head_range(n_heads: int, world: int, rank: int, kv_group: int = 1) -> range:
+    """Contiguous block of query heads owned by `rank`.  The n_heads / kv_group KV
+    heads are split in blocks that differ in size by at most one, and a rank owns the
+    kv_group query heads of each of its KV heads."""
     if world < 1 or not 0 <= rank < world:
         raise ValueError(f"rank {rank} outside a world of {world}")
-    base, extra = divmod(n_heads, world)
+    if kv_group < 1 or n_heads % kv_group:
+        raise ValueError(f"{n_heads} heads do not split into groups of {kv_group}")
+    base, extra = divmod(n_heads // kv_group, world)
     lo = rank * base + min(rank, extra)
-    return range(lo, lo + base + (1 if rank < extra else 0))
+    return range(lo * kv_group, (lo + base + (1 if rank < extra else 0)) * kv_group)
 
 
 def shard_bh(batch: int, n_heads: int, heads: range) -> torch.Tensor:
@@ -38,26 +44,37 @@ def shard_bh(batch: int, n_heads: int, heads: range) -> torch.Tensor:
 def shard_workload(wk: Workload, heads: range) -> Workload:
     """The rows of `heads` of a workload, as a workload of its own.
 
-    Q, context lengths, per-(batch, head) V scales and block-table rows are sliced;
-    a paged pool stays whole (the table rows point into it), a contiguous cache is
-    cut to the selected rows.  The worklist is rebuilt over the local rows."""
-    H = wk.heads
-    rows = shard_bh(wk.batch, H, heads).to(wk.q.device)
-    nb = len(rows)
+    Q rows are sliced by query head; context lengths, per-(batch, head) V scales and
+    block-table rows by KV head (the same thing without grouped-query heads).  A paged
+    pool stays whole (the table rows point into it), a contiguous cache is cut to the
+    selected KV rows.  The worklist is rebuilt over the local query rows."""
+    H, g = wk.heads, wk.kv_group
+    if heads.start % g or len(heads) % g:
+        raise ValueError(f"heads {heads.start}-{heads.stop - 1} are not whole groups of {g}")
+    Hkv = H // g
+    kv_heads = range(heads.start // g, heads.stop // g)
+    dev = wk.q.device
+    rows = shard_bh(wk.batch, H, heads).to(dev)
+    kv_rows = shard_bh(wk.batch, Hkv, kv_heads).to(dev)
+    nb, nkv = len(rows), len(kv_rows)
     q = wk.q.view(wk.n_bh, wk.seq_q, -1)[rows].reshape(nb * wk.seq_q, -1)
-    ctx = wk.ctx_lens[rows]
+    ctx = wk.ctx_lens[kv_rows]
     vs = wk.v_scale
-    if vs.numel() == wk.n_bh:
-        vs = vs[rows]
-    elif vs.numel() == H:
-        vs = vs[torch.tensor(list(heads), dtype=torch.int64, device=vs.device)]
+    pool_rows = wk.v.shape[0]
+    per_slot = vs.numel() == pool_rows and vs.numel() > 1
+    if not per_slot and vs.numel() == wk.n_kv_bh:
+        vs = vs[kv_rows]
+    elif not per_slot and vs.numel() == Hkv:
+        vs = vs[torch.tensor(list(kv_heads), dtype=torch.int64, device=vs.device)]
     if wk.block_tables.numel():
-        bt = wk.block_tables.view(wk.n_bh, -1)[rows].contiguous()
+        bt = wk.block_tables.view(wk.n_kv_bh, -1)[kv_rows].contiguous()
         k, v = wk.k, wk.v
     else:
         span = wk.num_blocks * wk.block_size
-        k = wk.k.view(wk.n_bh, span, -1)[rows].reshape(nb * span, -1)
-        v = wk.v.view(wk.n_bh, span, -1)[rows].reshape(nb * span, -1)
+        k = wk.k.view(wk.n_kv_bh, span, -1)[kv_rows].reshape(nkv * span, -1)
+        v = wk.v.view(wk.n_kv_bh, span, -1)[kv_rows].reshape(nkv * span, -1)
+        if per_slot:
+            vs = vs.view(wk.n_kv_bh, span)[kv_rows].reshape(-1)
         bt = wk.block_tables
     wl = dense_worklist(nb, wk.seq_q, wk.q.device)
     if wk.seq_q == 1:
@@ -66,20 +83,22 @@ def shard_workload(wk: Workload, heads: range) -> Workload:
                     k=k.contiguous(), v=v.contiguous(), v_scale=vs.contiguous(), ctx_lens=ctx.contiguous(),
                     block_tables=bt, seq_q=wk.seq_q, head_dim=wk.head_dim, block_size=wk.block_size,
                     num_blocks=wk.num_blocks, causal=wk.causal, o_dtype=wk.o_dtype, batch=wk.batch,
-                    heads=len(heads), inv_sqrt_d=wk.inv_sqrt_d, meta=dict(wk.meta))
+                    heads=len(heads), inv_sqrt_d=wk.inv_sqrt_d, meta=dict(wk.meta), kv_group=g)
 
 
-def assemble_heads(parts: List[torch.Tensor], batch: int, n_heads: int, seq_q: int, world: int) -> torch.Tensor:
+def assemble_heads(parts: List[torch.Tensor], batch: int, n_heads: int, seq_q: int, world: int,
+                   kv_group: int = 1) -> torch.Tensor:
     """Full O [batch*H*seq_q, D] from the ranks' head-block outputs, in rank order."""
     d = parts[0].shape[-1]
     out = torch.empty(batch, n_heads, seq_q, d, dtype=parts[0].dtype, device=parts[0].device)
     for r, part in enumerate(parts):
-        hr = head_range(n_heads, world, r)
+        hr = head_range(n_heads, world, r, kv_group)
         out[:, hr.start:hr.stop] = part.reshape(batch, len(hr), seq_q, d)
     return out.reshape(batch * n_heads * seq_q, d)
 
 
-def gather_output(o_local: torch.Tensor, batch: int, n_heads: int, seq_q: int, group=None) -> torch.Tensor:
+def gather_output(o_local: torch.Tensor, batch: int, n_heads: int, seq_q: int, group=None,
+                  kv_group: int = 1) -> torch.Tensor:
     """All-gathers the head-block outputs of every rank into the full O on each rank.
 
     Blocks of unequal size are padded to the largest for the collective.  Every rank
@@ -88,10 +107,10 @@ def gather_output(o_local: torch.Tensor, batch: int, n_heads: int, seq_q: int, g
 
     world = dist.get_world_size(group)
     d = o_local.shape[-1]
-    rows_max = batch * len(head_range(n_heads, world, 0)) * seq_q
+    rows_max = batch * len(head_range(n_heads, world, 0, kv_group)) * seq_q
     buf = torch.zeros(rows_max, d, dtype=o_local.dtype, device=o_local.device)
     buf[: o_local.shape[0]] = o_local
     bufs = [torch.empty_like(buf) for _ in range(world)]
     dist.all_gather(bufs, buf, group=group)
-    parts = [bufs[r][: batch * len(head_range(n_heads, world, r)) * seq_q] for r in range(world)]
-    return assemble_heads(parts, batch, n_heads, seq_q, world)
+    parts = [bufs[r][: batch * len(head_range(n_heads, world, r, kv_group)) * seq_q] for r in range(world)]
+    return assemble_heads(parts, batch, n_heads, seq_q, world, kv_group)

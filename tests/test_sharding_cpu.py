@@ -35,21 +35,46 @@ def _small_workloads():
         W.make_dense("d", 2, 5, 40, 40, causal=True, scale_mode="head", o_dtype=torch.float32, seed=31),
         W.make_dense("b", 2, 3, 1, 300, scale_mode="bh", o_dtype=torch.float32, seed=32),
         W.make_paged("p", 3, 4, [17, 64, 130], page=16, seed=33, o_dtype=torch.float32),
+        # grouped-query heads: 12 query heads over 3 KV heads, and 8 over 2 (paged)
+        W.make_dense("gqa_d", 2, 12, 1, 200, scale_mode="bh", o_dtype=torch.float32, seed=34, kv_heads=3),
+        W.make_paged("gqa_p", 2, 8, [40, 150], page=16, seed=35, o_dtype=torch.float32, kv_heads=2),
     ]
+
+
+def _shard(wk, world, rank):
+    return S.shard_workload(wk, S.head_range(wk.heads, world, rank, wk.kv_group))
+
+
+def test_head_range_keeps_kv_groups_whole():
+    for n_heads, g, world in ((32, 4, 8), (32, 4, 3), (12, 3, 2), (8, 8, 1)):
+        ranges = [S.head_range(n_heads, world, r, g) for r in range(world)]
+        assert ranges[0].start == 0 and ranges[-1].stop == n_heads
+        assert all(a.stop == b.start for a, b in zip(ranges, ranges[1:]))
+        assert all(r.start % g == 0 and len(r) % g == 0 for r in ranges)
+        sizes = [len(r) // g for r in ranges]
+        assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        S.head_range(30, 2, 0, 4)
+    wk = W.make_dense("g", 1, 8, 1, 32, o_dtype=torch.float32, kv_heads=2)
+    with pytest.raises(ValueError):
+        S.shard_workload(wk, range(0, 2))  # half a KV group
 
 
 @pytest.mark.parametrize("world", [2, 3])
 def test_shard_then_assemble_matches_full(oracle, world):
     for wk in _small_workloads():
+        if wk.heads // wk.kv_group < world:
+            continue
         full, _, err, _ = oracle.forward_workload_c(wk)
         assert err == 0
         parts = []
         for r in range(world):
-            sub = S.shard_workload(wk, S.head_range(wk.heads, world, r))
+            sub = _shard(wk, world, r)
+            assert sub.kv_group == wk.kv_group
             o, _, err, _ = oracle.forward_workload_c(sub)
             assert err == 0
             parts.append(torch.from_numpy(o))
-        got = S.assemble_heads(parts, wk.batch, wk.heads, wk.seq_q, world).numpy()
+        got = S.assemble_heads(parts, wk.batch, wk.heads, wk.seq_q, world, wk.kv_group).numpy()
         assert np.array_equal(got, full), wk.name
 
 
@@ -69,9 +94,9 @@ def _rank_main(rank, world, port, out_dir):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         for i, wk in enumerate(_small_workloads()):
-            sub = S.shard_workload(wk, S.head_range(wk.heads, world, rank))
+            sub = _shard(wk, world, rank)
             o, _, err, _ = O.forward_workload_c(sub, nthreads=1)
-            full = S.gather_output(torch.from_numpy(o), wk.batch, wk.heads, wk.seq_q)
+            full = S.gather_output(torch.from_numpy(o), wk.batch, wk.heads, wk.seq_q, kv_group=wk.kv_group)
             np.save(os.path.join(out_dir, f"r{rank}_w{i}.npy"), full.numpy())
             np.save(os.path.join(out_dir, f"r{rank}_w{i}_err.npy"), np.array([err]))
     finally:
