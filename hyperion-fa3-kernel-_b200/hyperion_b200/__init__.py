@@ -128,6 +128,7 @@ def hyperion_apex_kernel(
     for up to 4 consecutive work items on the same KV row.
     """
     total_work = int(total_work)
+    _check(int(kv_group) >= 1, "kv_group must be >= 1")
     _check(O.is_cuda, "O must be a CUDA tensor")
     dev = O.device
     for name, t in (("worklist", worklist), ("Q", Q), ("K_cache", K_cache), ("V_cache", V_cache),
@@ -144,7 +145,6 @@ def hyperion_apex_kernel(
     _check(O.is_contiguous(), "O must be contiguous")
     _check(head_dim in (128, 256), "head_dim must be 128 or 256")
     _check(k_packed_bytes == head_dim // 8, "k_packed_bytes must be head_dim // 8 (sign-bit K)")
-    _check(int(kv_group) >= 1, "kv_group must be >= 1")
     n_kv = context_lens.numel()
     n_bh = n_kv * int(kv_group)
     row_bytes = head_dim // 8

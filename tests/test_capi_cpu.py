@@ -72,3 +72,29 @@ def test_c_boundary_rejects_bad_sizes_without_touching_the_device(hyperion):
     args[19] = fake
     args[18] = ctypes.byref(ext_bad)
     assert lib.hyperion_apex_kernel(*args) == _capi.HYPERION_ERR_INVALID_ARG
+
+
+def test_c_boundary_rejects_bad_kv_group_without_touching_the_device(hyperion):
+    from hyperion_b200 import _capi
+
+    lib = _capi.lib
+    ext = _capi.Extents(1, 16, 1, 0, _capi.DTYPE_F32, 0, 0, 0)
+    fake = ctypes.c_void_p(256)
+
+    def call(opt, ext_):
+        return lib.hyperion_apex_kernel_ex(fake, 1, fake, None, fake, None, fake, fake, fake, None, fake, 1, 128, 16,
+                                           16, 1, ctypes.c_float(0.088), 0, ctypes.byref(ext_), ctypes.byref(opt),
+                                           fake, 1 << 20, None)
+
+    assert call(_capi.Options(0, 0, None, 0, -1), ext) == _capi.HYPERION_ERR_INVALID_ARG
+    assert "kv_group" in _capi.last_error()
+    big = _capi.Extents(1 << 28, 16, 1, 0, _capi.DTYPE_F32, 0, 0, 0)
+    assert call(_capi.Options(0, 0, None, 0, 16), big) == _capi.HYPERION_ERR_INVALID_ARG
+    assert "kv_group" in _capi.last_error()
+
+
+def test_python_boundary_checks_kv_group(hyperion):
+    t = torch.zeros(4, 4, dtype=torch.int32)
+    with pytest.raises(RuntimeError, match="kv_group"):
+        hyperion.hyperion_apex_kernel(t, 4, t, None, t, None, t.to(torch.uint8), torch.ones(1), t[0],
+                                      None, torch.zeros(4, 128), 1, 128, 16, 16, 1, 0.088, False, kv_group=0)
