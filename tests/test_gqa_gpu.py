@@ -67,9 +67,9 @@ def test_gqa_paged_decode(hyperion, oracle, num_splits):
 
 def test_gqa_equals_block_tables_repeated_per_query_head(hyperion, oracle):
     """The same problem given to the ungrouped kernel, every query head's block-table
-    row pointing at its KV head's pages.  Both meet the bar against the oracle; they
-    differ only by rounding (the grouped kernel accumulates f16 products on the tensor
-    cores in f32, the ungrouped one sums 16-key groups of f16x2 products first)."""
+    row pointing at its KV head's pages.  Both meet the bar against the oracle, and
+    they agree with each other to rounding: both kernels sum the same 16-key groups of
+    f16x2 products, so any difference comes from a different split of the keys."""
     wk = W.make_paged("gqa_eq", 3, 8, [100, 999, 3000], page=16, seed=53, o_dtype=torch.float32, kv_heads=2)
     o_g, err, _, _ = run(hyperion, wk, path="row", num_splits=2)
     assert err == 0
@@ -177,3 +177,36 @@ def test_gqa_cache_written_per_kv_head_then_read(hyperion, oracle):
     o, err, _, _ = run(hyperion, wk, path="row")
     assert err == 0
     check(oracle, wk, o)
+
+
+def _paged_kv_copy(wk, page=16, seed=0):
+    """The same keys as a contiguous grouped-query workload, moved into a shuffled
+    pool of pages (one block-table row per KV row)."""
+    n_kv = wk.n_kv_bh
+    S = wk.block_size
+    pages = (S + page - 1) // page
+    g = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(n_kv * pages, generator=g)
+    k = torch.zeros(n_kv * pages * page, wk.k.shape[1], dtype=wk.k.dtype)
+    v = torch.zeros(n_kv * pages * page, wk.head_dim, dtype=wk.v.dtype)
+    bt = torch.zeros(n_kv, pages, dtype=torch.int32)
+    for r in range(n_kv):
+        for pg in range(pages):
+            blk = int(perm[r * pages + pg])
+            lo, hi = pg * page, min(S, (pg + 1) * page)
+            k[blk * page: blk * page + hi - lo] = wk.k[r * S + lo: r * S + hi]
+            v[blk * page: blk * page + hi - lo] = wk.v[r * S + lo: r * S + hi]
+            bt[r, pg] = blk
+    return W.Workload(**{**wk.__dict__, "k": k, "v": v, "block_tables": bt, "block_size": page,
+                         "num_blocks": pages})
+
+
+@pytest.mark.parametrize("path", ["tile", "row"])
+def test_gqa_paged_causal_prefill(hyperion, oracle, path):
+    dense = W.make_dense("gqa_pp", 2, 8, 200, 200, causal=True, scale_mode="head", o_dtype=torch.float32, seed=64,
+                         kv_heads=2)
+    wk = _paged_kv_copy(dense, page=16, seed=3)
+    o, err, _, info = run(hyperion, wk, path=path)
+    assert err == 0 and info["path"] == path
+    check(oracle, wk, o)
+    check(oracle, dense, o)
