@@ -69,7 +69,7 @@ int setup_group(int& ctas, int& smem) {
   cudaError_t e =
       cudaFuncSetAttribute(hyp::row::row_group_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(row group)");
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, hyp::row::row_group_kernel<D>, hyp::row::kThreads, smem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, hyp::row::row_group_kernel<D>, hyp::row::kGThreads, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor(row group)");
   if (ctas < 1) ctas = 1;
   return HYPERION_OK;
@@ -311,9 +311,9 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
     const int smem = (head_dim == 256) ? di->group_smem_256 : di->group_smem_128;
     grid = (int)std::min<long long>(gunits, (long long)di->n_sm * ctas);
     if (head_dim == 256) {
-      hyp::row::row_group_kernel<256><<<grid, hyp::row::kThreads, smem, st>>>(p, (int)gunits);
+      hyp::row::row_group_kernel<256><<<grid, hyp::row::kGThreads, smem, st>>>(p, (int)gunits);
     } else {
-      hyp::row::row_group_kernel<128><<<grid, hyp::row::kThreads, smem, st>>>(p, (int)gunits);
+      hyp::row::row_group_kernel<128><<<grid, hyp::row::kGThreads, smem, st>>>(p, (int)gunits);
     }
   } else {
     const int ctas = (head_dim == 256) ? di->row_ctas_256 : di->row_ctas_128;

@@ -24,6 +24,11 @@ namespace hyp {
 namespace row {
 
 constexpr int kGroupMax = 4;  // queries per run
+// Warp layout: a producer warp and 4 consumer warps, each consumer owning 16 keys
+// of every 64-key stage (lanes 0-15 score one key each).
+constexpr int kGWarps = 4;
+constexpr int kGKeysPerWarp = kKeysPerStage / kGWarps;  // 16
+constexpr int kGThreads = 32 * (1 + kGWarps);
 // KV ring depth: 3 stages for head_dim 128 (6 CTAs of them fit an SM's shared
 // memory), 2 for head_dim 256 (4 CTAs).
 template <int D>
@@ -54,10 +59,10 @@ struct GroupSmem {
   alignas(128) uint8_t v[NS][kVBytes];
   StageHeader hdr[NS];
   RunSlot<W> slot[2];
-  float merge_m[kConsumerWarps];
-  float merge_l[kConsumerWarps];
-  float merge_acc[kConsumerWarps][D];
-  alignas(16) uint32_t wbuf[kConsumerWarps][kGroupMax][kKeysPerWarp];  // f16x2 {w, w} per query and key
+  float merge_m[kGWarps];
+  float merge_l[kGWarps];
+  float merge_acc[kGWarps][D];
+  alignas(16) uint32_t wbuf[kGWarps][kGroupMax][kGKeysPerWarp];  // f16x2 {w, w} per query and key
   alignas(8) uint64_t full[NS];
   alignas(8) uint64_t empty[NS];
   alignas(8) uint64_t run_full[2];
@@ -74,7 +79,7 @@ template <int D>
 constexpr int group_ctas() { return D == 128 ? 6 : 4; }
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, group_ctas<D>()) row_group_kernel(FwdParams p, int total_units) {
+__global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(FwdParams p, int total_units) {
   constexpr int W = D / 32;
   constexpr int DPL = D / 32;  // dims per lane
   constexpr int NW = DPL / 4;  // 32-bit words of V bytes per lane and key
@@ -91,18 +96,18 @@ __global__ void __launch_bounds__(kThreads, group_ctas<D>()) row_group_kernel(Fw
   // fence orders these stores before the bulk copies that overwrite them.
   {
     uint4* v4 = reinterpret_cast<uint4*>(&sm.v[0][0]);
-    for (int i = threadIdx.x; i < kGStages * GroupSmem<D>::kVBytes / 16; i += kThreads)
+    for (int i = threadIdx.x; i < kGStages * GroupSmem<D>::kVBytes / 16; i += kGThreads)
       v4[i] = make_uint4(0u, 0u, 0u, 0u);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGStages; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], kConsumerWarps);
+      mbar_init(&sm.empty[s], kGWarps);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.run_full[s], 1);
-      mbar_init(&sm.run_empty[s], kConsumerWarps);
+      mbar_init(&sm.run_empty[s], kGWarps);
     }
     sm.abort = 0;
     fence_mbar_init();
@@ -294,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, group_ctas<D>()) row_group_kernel(Fw
           constexpr int JN = (NQ == 0) ? G : NQ;  // query slots the loops visit
           const int nk = sm.hdr[s].nkeys;
           const unsigned long long mask = sm.hdr[s].mask;
-          const int jl = cw * kKeysPerWarp + (lane & 15);
+          const int jl = cw * kGKeysPerWarp + (lane & 15);
           const int key = k0 + jl;
           const bool okk = (lane < 16) && (jl < nk) && ((mask >> jl) & 1ull);
           uint32_t kr[W];
@@ -364,12 +369,12 @@ __global__ void __launch_bounds__(kThreads, group_ctas<D>()) row_group_kernel(Fw
               if (ok_all[j]) p.debug_scores[(long long)sl.item[j] * p.debug_ld + key] = si_all[j];
           }
           if (!any_all) return;
-          const uint8_t* vbase = &sm.v[s][(cw * kKeysPerWarp) * D];
+          const uint8_t* vbase = &sm.v[s][(cw * kGKeysPerWarp) * D];
           bool exact = p.v_scale_mode == 2;
           if (!exact) {
             // f16x2 products of the hardware decode, shared by the run's queries;
             // see row_fwd_kernel for the ranges and the NaN rule.
-            if (lane < kKeysPerWarp) {
+            if (lane < kGKeysPerWarp) {
 #pragma unroll
               for (int j = 0; j < JN; ++j) sm.wbuf[cw][j][lane] = pack_f16x2(w[j], w[j]);
             }
@@ -381,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, group_ctas<D>()) row_group_kernel(Fw
               for (int i = 0; i < NW; ++i) plo[j][i] = phi[j][i] = 0u;
             }
 #pragma unroll
-            for (int j2 = 0; j2 < kKeysPerWarp; j2 += 2) {
+            for (int j2 = 0; j2 < kGKeysPerWarp; j2 += 2) {
               uint2 wp[JN];
 #pragma unroll
               for (int j = 0; j < JN; ++j) wp[j] = *reinterpret_cast<const uint2*>(&sm.wbuf[cw][j][j2]);
@@ -444,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, group_ctas<D>()) row_group_kernel(Fw
 #pragma unroll
             for (int j = 0; j < JN; ++j) ws[j] = w[j] * vsl * kTwoPow120;
 #pragma unroll 2
-            for (int jj = 0; jj < kKeysPerWarp; ++jj) {
+            for (int jj = 0; jj < kGKeysPerWarp; ++jj) {
               float wk[JN];
               bool nz = false;
 #pragma unroll
@@ -492,22 +497,22 @@ __global__ void __launch_bounds__(kThreads, group_ctas<D>()) row_group_kernel(Fw
           }
 #pragma unroll
           for (int i = 0; i < DPL; ++i) sm.merge_acc[cw][lane * DPL + i] = acc[j][i];
-          named_bar_sync(1, 32 * kConsumerWarps);
+          named_bar_sync(1, 32 * kGWarps);
           float M = -INFINITY;
 #pragma unroll
-          for (int w2 = 0; w2 < kConsumerWarps; ++w2) M = fmaxf(M, sm.merge_m[w2]);
-          float f[kConsumerWarps];
+          for (int w2 = 0; w2 < kGWarps; ++w2) M = fmaxf(M, sm.merge_m[w2]);
+          float f[kGWarps];
           float L = 0.f;
 #pragma unroll
-          for (int w2 = 0; w2 < kConsumerWarps; ++w2) {
+          for (int w2 = 0; w2 < kGWarps; ++w2) {
             const float mw = sm.merge_m[w2];
             f[w2] = (mw == -INFINITY) ? 0.f : exp_clamped(mw - M);
             L += sm.merge_l[w2] * f[w2];
           }
-          for (int d = cw * 32 + lane; d < D; d += 32 * kConsumerWarps) {
+          for (int d = cw * 32 + lane; d < D; d += 32 * kGWarps) {
             float a = 0.f;
 #pragma unroll
-            for (int w2 = 0; w2 < kConsumerWarps; ++w2) a += sm.merge_acc[w2][d] * f[w2];
+            for (int w2 = 0; w2 < kGWarps; ++w2) a += sm.merge_acc[w2][d] * f[w2];
             a *= vs_run;
             if (stop) continue;
             if (p.n_split == 1) {
@@ -522,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, group_ctas<D>()) row_group_kernel(Fw
               }
             }
           }
-          named_bar_sync(1, 32 * kConsumerWarps);
+          named_bar_sync(1, 32 * kGWarps);
         }
       }
       __syncwarp();
