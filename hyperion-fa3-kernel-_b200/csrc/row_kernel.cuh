@@ -12,10 +12,10 @@
 //     replacing the cp.async 16 B copies and the 6-stage ring (:377-452);
 //   * per page, the block table gives the pool block (:402-411); a page id outside
 //     the pool raises HYPERION_DEVERR_BAD_BLOCK and its keys are skipped;
-//   * consumers: 4 warps, each owning a quarter of every stage's keys with its own
+//   * consumers: 2 warps, each owning half of every stage's keys with its own
 //     running (m, l, acc); the score is D - 2*popcount(q XOR k) (README.md:22),
 //     the softmax the reference's clamped online update (:544-572) applied per
-//     16-key group, and the FP8 decode the hardware e4m3 conversion, which agrees
+//     32-key group, and the FP8 decode the hardware e4m3 conversion, which agrees
 //     with the reference's rule (:122-141) on every code but 0x7F / 0xFF; a group
 //     that holds one of those is redone with the rule itself, as bit moves;
 //   * the four per-warp states are merged through shared memory, then either
@@ -30,14 +30,18 @@ namespace hyp {
 namespace row {
 
 constexpr int kKeysPerStage = 64;
-// Two 64-key stages per CTA and 8 CTAs per SM: on B200 more resident CTAs with a
+// Two 64-key stages per CTA and 11 CTAs per SM: on B200 more resident CTAs with a
 // shallow ring hide the HBM latency better than fewer CTAs with a deep one
-// (decode B64 H32 S_kv 8192: 2 x 8 reaches 84 % of the measured copy bandwidth,
-// 4 x 5 reaches 76 %).
+// (decode B64 H32 S_kv 8192, 4 consumer warps: 2 stages x 8 CTAs reached 84 % of
+// the measured copy bandwidth, 4 x 5 reached 76 %).  Two consumer warps of 32 keys
+// each, rather than four of 16, put all 32 lanes on the scores and spread each
+// group's softmax step over twice the keys; under the sustained power cap that
+// took the same decode from 0.42 to 0.37 ms (0.87 to 0.99 of the copy bandwidth).
 constexpr int kStages = 2;
-constexpr int kConsumerWarps = 4;
+constexpr int kConsumerWarps = 2;
 constexpr int kThreads = 32 * (1 + kConsumerWarps);
-constexpr int kKeysPerWarp = kKeysPerStage / kConsumerWarps;  // 16
+constexpr int kKeysPerWarp = kKeysPerStage / kConsumerWarps;  // 32
+constexpr int kRowCtasPerSm = 11;  // the register budget; shared memory allows 11
 
 struct StageHeader {
   int nkeys;
@@ -96,7 +100,7 @@ __device__ __forceinline__ void load_v_lane(const uint8_t* row, int lane, uint32
 }
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 8) row_fwd_kernel(FwdParams p, int total_units) {
+__global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdParams p, int total_units) {
   constexpr int W = D / 32;
   constexpr int DPL = D / 32;  // dims per lane
   constexpr int NW = DPL / 4;  // 32-bit words of V bytes per lane and key
@@ -276,8 +280,8 @@ __global__ void __launch_bounds__(kThreads, 8) row_fwd_kernel(FwdParams p, int t
         }
         const int n = sm.hdr[s].nkeys;
         const unsigned long long mask = sm.hdr[s].mask;
-        const int jl = cw * kKeysPerWarp + (lane & 15);
-        const bool ok = (lane < 16) && (jl < n) && ((mask >> jl) & 1ull);
+        const int jl = cw * kKeysPerWarp + (lane % kKeysPerWarp);
+        const bool ok = (lane < kKeysPerWarp) && (jl < n) && ((mask >> jl) & 1ull);
         int si = 0;
         if (ok) {
           const uint32_t* kr = reinterpret_cast<const uint32_t*>(&sm.k[s][jl * W * 4]);
@@ -309,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 8) row_fwd_kernel(FwdParams p, int t
           bool exact = p.v_scale_mode == 2;
           if (!exact) {
             // Products on f16x2: w in [0, 1] and |V| <= 448, so the sums over this
-            // warp's 16 keys stay below 16 * 448 = 7168, inside the f16 range; they
+            // warp's 32 keys stay below 32 * 448 = 14336, inside the f16 range; they
             // are added to the f32 accumulators once per stage.  A key that is
             // absent has w = 0, so its products are 0 unless its bytes decode to NaN.
             if (lane < kKeysPerWarp) sm.wbuf[cw][lane] = pack_f16x2(w, w);
@@ -389,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 8) row_fwd_kernel(FwdParams p, int t
       // when it gave up on a wait: the barriers have no timeout of their own.
       const bool stop = aborted || (*abort != 0);
 
-      // ---- merge the four warps' (m, l, acc) ----
+      // ---- merge the consumer warps' (m, l, acc) ----
       const float l_warp = warp_sum(l);
       if (lane == 0) {
         sm.merge_m[cw] = m;
