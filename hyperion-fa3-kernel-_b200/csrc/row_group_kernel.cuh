@@ -24,15 +24,18 @@ namespace hyp {
 namespace row {
 
 constexpr int kGroupMax = 4;  // queries per run
-// Warp layout: a producer warp and 4 consumer warps, each consumer owning 16 keys
-// of every 64-key stage (lanes 0-15 score one key each).
-constexpr int kGWarps = 4;
-constexpr int kGKeysPerWarp = kKeysPerStage / kGWarps;  // 16
+// Warp layout: a producer warp and 2 consumer warps, each consumer owning 32 keys
+// of every 64-key stage (every lane scores one key against all queries of the run).
+// Against 4 consumer warps of 16 keys, this keeps whole warps on the scores and
+// pays each group's softmax step per 32 keys: decode with 32 query heads over 8 KV
+// heads went from 0.232 to 0.179 ms.
+constexpr int kGWarps = 2;
+constexpr int kGKeysPerWarp = kKeysPerStage / kGWarps;  // 32
 constexpr int kGThreads = 32 * (1 + kGWarps);
-// KV ring depth: 3 stages for head_dim 128 (6 CTAs of them fit an SM's shared
-// memory), 2 for head_dim 256 (4 CTAs).
+// KV ring depth: 2 stages, so that 10 CTAs (head_dim 128) or 5 (head_dim 256) fit
+// an SM's shared memory.
 template <int D>
-constexpr int group_stages() { return D == 128 ? 3 : 2; }
+constexpr int group_stages() { return 2; }
 
 template <int W>
 struct RunSlot {
@@ -71,12 +74,10 @@ struct GroupSmem {
 };
 
 // Resident CTAs per SM the register budget is set for.  The kernel is bound by
-// instruction issue and latency rather than HBM, so more resident warps pay: for
-// head_dim 128, 6 CTAs (64 registers, a few bytes spilled) ran decode with 32 query
-// heads over 8 KV heads in 0.245 ms where 5 CTAs (72, none) took 0.254 ms and 4
-// CTAs 0.258 ms; head_dim 256 needs 96 registers (4 CTAs).
+// instruction issue and latency rather than HBM, so resident warps pay: head_dim
+// 128 runs 10 CTAs at 64 registers (a few bytes spilled), head_dim 256 runs 5.
 template <int D>
-constexpr int group_ctas() { return D == 128 ? 6 : 4; }
+constexpr int group_ctas() { return D == 128 ? 10 : 5; }
 
 template <int D>
 __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(FwdParams p, int total_units) {
@@ -299,9 +300,9 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
           constexpr int JN = (NQ == 0) ? G : NQ;  // query slots the loops visit
           const int nk = sm.hdr[s].nkeys;
           const unsigned long long mask = sm.hdr[s].mask;
-          const int jl = cw * kGKeysPerWarp + (lane & 15);
+          const int jl = cw * kGKeysPerWarp + (lane % kGKeysPerWarp);
           const int key = k0 + jl;
-          const bool okk = (lane < 16) && (jl < nk) && ((mask >> jl) & 1ull);
+          const bool okk = (lane < kGKeysPerWarp) && (jl < nk) && ((mask >> jl) & 1ull);
           uint32_t kr[W];
 #pragma unroll
           for (int i = 0; i < W; ++i) kr[i] = 0u;
