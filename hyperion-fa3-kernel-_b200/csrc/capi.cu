@@ -123,16 +123,37 @@ int choose_splits(const DevInfo& di, int D, int total_work, long long max_keys) 
   return (int)std::max<long long>(ns, 1);
 }
 
+// KV splits per unit of the grouped row kernel, whose unit holds up to 4 work
+// items: enough units for 4 per CTA slot and, while units are scarce (fewer than
+// 16 per slot), pieces of at most 2048 keys so that ragged contexts balance; no
+// piece shorter than 512 keys, at most 16 pieces.  (Paged decode with 32 query
+// heads over 8 KV heads, contexts U[512, 32768]: 1.21 ms at 13-16 pieces against
+// 1.27 ms at the row kernel's choice of 4 in isolated calls; the same 1.26 ms under
+// the sustained power cap, where the whole step with host copies gains 4 %.)
+int choose_group_splits(const DevInfo& di, int D, long long chunks, long long max_keys) {
+  if (chunks <= 0) return 1;
+  const long long slots = (long long)di.n_sm * ((D == 256) ? di.group_ctas_256 : di.group_ctas_128);
+  if (chunks >= 16 * slots) return 1;
+  long long ns = (4 * slots + chunks - 1) / chunks;
+  ns = std::max(ns, (max_keys + 2047) / 2048);
+  ns = std::min(ns, std::max<long long>(1, max_keys / 512));
+  ns = std::min<long long>(ns, 16);
+  return (int)std::max<long long>(ns, 1);
+}
+
 size_t partial_bytes(int total_work, int n_split, int D) {
   if (n_split <= 1) return 0;
   return (size_t)total_work * n_split * (2 + D) * sizeof(float);
 }
 
-// Workspace of the automatic split choice (a forced num_splits needs
-// 256 + total_work * num_splits * (2 + head_dim) * 4 bytes).
+// Workspace of the automatic split choice, for either row kernel (a forced
+// num_splits needs 256 + total_work * num_splits * (2 + head_dim) * 4 bytes).
+// The grouped kernel's choice is bounded by its smallest unit count, 4 items a unit.
 size_t workspace_needed(const DevInfo& di, int total_work, int D, int block_size, int num_blocks) {
   const long long max_keys = (long long)std::max(block_size, 1) * std::max(num_blocks, 1);
-  return hyp::kWsPartials + partial_bytes(total_work, choose_splits(di, D, total_work, max_keys), D);
+  const int ns = std::max(choose_splits(di, D, total_work, max_keys),
+                          choose_group_splits(di, D, ((long long)total_work + 3) / 4, max_keys));
+  return hyp::kWsPartials + partial_bytes(total_work, ns, D);
 }
 
 }  // namespace
@@ -291,20 +312,23 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
     return HYPERION_OK;
   }
 
-  int ns = (opt && opt->num_splits > 0) ? std::min(opt->num_splits, 16) : choose_splits(*di, head_dim, total_work, max_keys);
+  // Grouped row kernel: a unit is up to 4 consecutive work items and one KV
+  // split, and a run of them on one KV row streams its keys once: the query heads
+  // of one KV head (grouped-query attention), or neighbouring query rows of one
+  // (batch, head) in a prefill worklist.
+  const bool grouped = kv_group > 1 || seq_q > 1;
+  p.group_items = !grouped ? 1 : (kv_group > 1) ? std::min(kv_group, hyp::row::kGroupMax) : hyp::row::kGroupMax;
+  const long long chunks = ((long long)total_work + p.group_items - 1) / p.group_items;
+  int ns = (opt && opt->num_splits > 0) ? std::min(opt->num_splits, 16)
+           : grouped                    ? choose_group_splits(*di, head_dim, chunks, max_keys)
+                                        : choose_splits(*di, head_dim, total_work, max_keys);
   const size_t need = hyp::kWsPartials + partial_bytes(total_work, ns, head_dim);
   if (workspace_bytes < need) return fail(HYPERION_ERR_WORKSPACE, "workspace smaller than hyperion_workspace_bytes()");
   p.n_split = ns;
   const long long units = (long long)total_work * ns;
   if (units > 0x7fffffffLL) return fail(HYPERION_ERR_UNSUPPORTED, "too many work units");
   int grid = 0;
-  if (kv_group > 1 || seq_q > 1) {
-    // Grouped row kernel: a unit is up to 4 consecutive work items and one KV
-    // split, and a run of them on one KV row streams its keys once: the query
-    // heads of one KV head (grouped-query attention), or neighbouring query rows
-    // of one (batch, head) in a prefill worklist.
-    p.group_items = (kv_group > 1) ? std::min(kv_group, hyp::row::kGroupMax) : hyp::row::kGroupMax;
-    const long long chunks = ((long long)total_work + p.group_items - 1) / p.group_items;
+  if (grouped) {
     const long long gunits = chunks * ns;
     if (gunits > 0x7fffffffLL) return fail(HYPERION_ERR_UNSUPPORTED, "too many work units");
     const int ctas = (head_dim == 256) ? di->group_ctas_256 : di->group_ctas_128;
@@ -492,7 +516,10 @@ extern "C" int hyperion_apex_kernel_noalloc(const int32_t* worklist, int32_t tot
     const DevInfo* di = nullptr;
     if (get_dev(&di) != HYPERION_OK) return rc;
     const long long max_keys = (long long)block_size * num_blocks;
-    const int ns = choose_splits(*di, head_dim, total_work, max_keys);
+    // The split count the forward chose: a query row per (batch, head) takes the
+    // row kernel, several take the grouped kernel (4 work items a unit).
+    const int ns = (seq_q > 1) ? choose_group_splits(*di, head_dim, ((long long)total_work + 3) / 4, max_keys)
+                               : choose_splits(*di, head_dim, total_work, max_keys);
     char msg[320];
     std::snprintf(msg, sizeof(msg),
                   "hyperion_apex_kernel_noalloc: this call needs %zu bytes of scratch (%d work items x %d KV splits "
