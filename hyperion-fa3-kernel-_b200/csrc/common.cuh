@@ -144,16 +144,8 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
 // Bulk copy global -> shared through the TMA engine (no tensor map: plain bytes).
 // Both addresses 16-byte aligned, size a multiple of 16.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
-                                         uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(smem_dst)),
-      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// Same copy with an L2 eviction-priority hint for data read once (KV streams).
+// The copy takes an L2 eviction-priority hint (evict-first for data read once,
+// the KV streams; evict-last for data read again).
 __device__ __forceinline__ void bulk_g2s_stream(void* smem_dst, const void* gmem_src, uint32_t bytes,
                                                 uint64_t* bar, uint64_t policy) {
   asm volatile(

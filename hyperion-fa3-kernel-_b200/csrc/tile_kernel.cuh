@@ -63,12 +63,6 @@ constexpr int kVBlockBytes = kKeys * 128;     // one 64-dim block (LBO of the V 
 // Lazy rescale threshold: P = exp(s - m) may grow to 2^8 before the running max
 // is moved (8 / log2(e) in score units), well inside the f16 range of P.
 constexpr float kTauS = 5.545177444479562f;
-// Integer scores of head_dim 128 lie in [-128, 128] and all have the parity of 128, so
-// a score minus the row's integer maximum is 2(j - 128) for a j in [0, 256].
-constexpr int kPTabRows = 257;
-// Odd columns' weights by table lookup instead of the exponential unit (the table
-// takes 33 KB of shared memory, which then has no room for a third KV stage).
-constexpr bool kPTable = false;
 
 struct UnitInfo {
   int kind;     // 0 stop, 1 work
@@ -80,7 +74,9 @@ struct UnitInfo {
   int ctx;      // clamped context length of bh
   int kv_len;   // keys [0, kv_len) are loaded
   int n_tiles;
-  int pad[3];
+  int kv;       // KV row of bh (bh / kv_group), resolved once per unit
+  float vs;     // V scale of the unit
+  int pad;
 };
 
 struct Smem {
@@ -93,7 +89,6 @@ struct Smem {
   // Softmax weights by table: entry j (one copy per lane, so a warp's lookups never
   // share a bank) holds exp(max(|c| * 2(j - 128), -80)), the weight of a score that
   // lies 2(j - 128) above the row's running integer maximum (|c| = |inv_sqrt_d|).
-  alignas(128) float ptab[kPTable ? kPTabRows : 1][32];
   uint32_t kv_mask[kKvStages][4];
   UnitInfo unit[2];
   alignas(8) uint64_t sched_full[2];
@@ -269,36 +264,20 @@ __device__ __forceinline__ float row_tile_max(uint32_t s_col, const uint32_t (&m
 }
 
 // The weight exp(|c| (S - S_m)) of an integer score S (exact in f32) relative to the
-// row's integer maximum S_m, computed two ways that agree to rounding: on the
-// exponential unit as 2^(S*k2 + bias) with bias = -S_m*k2, or by a lookup in the
-// table.  Alternating them keeps the exponential unit and the load/ALU pipes busy
-// together.  For the lookup, fmaf(S, 64, c) with c = 2^23 + 16384 - 64*S_m + 4*lane
-// is 2^23 plus the entry's byte offset (64 (S - S_m) + 16384 = 128 j, plus 4*lane for
-// this lane's copy), exact for every pair of scores, so the float's bits minus those
-// of 2^23 give the offset.
+// row's integer maximum S_m, on the exponential unit as 2^(S*k2 + bias) with
+// bias = -S_m*k2.
 struct PExp {
-  float k2, bias;  // exponential unit
-  float c;         // table: 2^23 + 16384 - 64*S_m + 4*lane
-  uint32_t a;      // table: shared address of entry 0 minus the bits of 2^23
+  float k2, bias;
 };
 
 __device__ __forceinline__ float pexp_mufu(uint32_t s, const PExp& x) {
   return ex2_approx(fmaf(__uint_as_float(s), x.k2, x.bias));
 }
-__device__ __forceinline__ float pexp_lut(uint32_t s, const PExp& x) {
-  const uint32_t addr = __float_as_uint(fmaf(__uint_as_float(s), 64.f, x.c)) + x.a;
-  float r;
-  asm("ld.shared.f32 %0, [%1];" : "=f"(r) : "r"(addr));
-  return r;
-}
 
-// Weights of one 16-column chunk: even columns on the exponential unit, odd ones by table.
+// Weights of one 16-column chunk.
 __device__ __forceinline__ void p_exp16(const uint32_t (&v)[16], const PExp& x, float (&e)[16]) {
 #pragma unroll
-  for (int i = 0; i < 16; i += 2) {
-    e[i] = pexp_mufu(v[i], x);
-    e[i + 1] = kPTable ? pexp_lut(v[i + 1], x) : pexp_mufu(v[i + 1], x);
-  }
+  for (int i = 0; i < 16; ++i) e[i] = pexp_mufu(v[i], x);
 }
 
 // Finishes chunk h (exponentials in `e`: mask, add to l[], pack to f16 pairs, store
@@ -313,7 +292,7 @@ __device__ __forceinline__ void p_step(uint32_t s_col, int h, float (&e)[16], ui
   for (int i = 0; i < 8; ++i) {
     if (kNext) {
       en[2 * i] = pexp_mufu(vn[2 * i], x);
-      en[2 * i + 1] = kPTable ? pexp_lut(vn[2 * i + 1], x) : pexp_mufu(vn[2 * i + 1], x);
+      en[2 * i + 1] = pexp_mufu(vn[2 * i + 1], x);
     }
     float e0 = e[2 * i], e1 = e[2 * i + 1];
     if (kMasked) {
@@ -426,11 +405,6 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     tc::tmem_alloc(&sm.tmem_base, kTmemCols);
     tc::tmem_relinquish();
   }
-  if (kPTable) {
-    const float cabs = fabsf(p.inv_sqrt_d);
-    for (int i = threadIdx.x; i < kPTabRows * 32; i += kThreads)
-      sm.ptab[i >> 5][i & 31] = expf(fmaxf(cabs * (float)(2 * ((i >> 5) - 128)), kExpClamp));
-  }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -509,7 +483,8 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           seg_lo = seg_hi;
           continue;
         }
-        int ctx = __ldg(p.ctx_lens + kv_of(p, bh0));
+        const int kv0 = kv_of(p, bh0);
+        int ctx = __ldg(p.ctx_lens + kv0);
         if (ctx < 0) {
           if (lane == 0) raise_error(p.err, HYPERION_DEVERR_NEG_CTX);
           ctx = 0;
@@ -532,6 +507,8 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           u.seg_lo = seg_lo;
           u.seg_hi = seg_hi;
           u.bh = bh0;
+          u.kv = kv0;
+          u.vs = (p.v_scale_mode == 0) ? __ldg(p.v_scale) : __ldg(p.v_scale + (kv0 % p.v_scale_numel));
           u.ctx = ctx;
           u.kv_len = kv_len;
           u.n_tiles = n_tiles;
@@ -554,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       ++uc;
       if (u.kind == 0) break;
       {
-        const int bh0 = u.bh;
+        const int kv0 = u.kv;
         const int kv_len = u.kv_len;
         const int n_tiles = u.n_tiles;
         for (int j = 0; j < n_tiles; ++j) {
@@ -574,7 +551,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
             const int page = p0 + i;
             const int lo = max(k0, page * bs) - k0;
             const int hi = min(k0 + n, (page + 1) * bs) - k0;
-            if (page_block_id(p, bh0, page) >= 0) {
+            if (page_block_id_kv(p, kv0, page) >= 0) {
               bytes += (uint32_t)(hi - lo) * (16u + 128u);
 #pragma unroll
               for (int w = 0; w < 4; ++w) {
@@ -605,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
             const int page = p0 + i;
             const int lo = max(k0, page * bs);
             const int hi = min(k0 + n, (page + 1) * bs);
-            const long long id = page_block_id(p, bh0, page);
+            const long long id = page_block_id_kv(p, kv0, page);
             if (id >= 0) {
               const long long slot0 = id * bs + (lo - page * bs);
               const uint32_t cnt = (uint32_t)(hi - lo);
@@ -824,7 +801,6 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     // Running max from which on a row needs no max pass: (head_dim * |inv_sqrt_d|)
     // minus 11, so exp(s - m) <= e^11 < 2^15.9 for every possible score s.
     const float m_safe = 128.f * cabs - 11.0f;
-    const uint32_t tab_addr = smem_u32(&sm.ptab[0][0]);
     uint32_t uc = 0, kvit = 0, oc = 0;
     // The next unit is taken from its slot, and the global load of this row's q_idx
     // issued, before the current unit's epilogue (the scheduler publishes units one
@@ -849,7 +825,6 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       const int q_idx = (n_qi >= 0 && n_qi < p.seq_q) ? n_qi : -1;
       const bool row_ok = q_idx >= 0;
       const int n_tiles = u.n_tiles;
-      const int bh = u.bh;
       const int item = u.entry0 + r;
       const long long o_base = row_ok ? ((long long)u.bh * p.seq_q + q_idx) * 128 : 0;
       const int row_end = row_ok ? (p.causal ? min(u.ctx, q_idx + 1) : u.ctx) : 0;
@@ -919,8 +894,6 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         PExp x;
         x.k2 = k2;
         x.bias = -(float)s_m * k2;
-        x.c = 8388608.f + (float)(16384 - 64 * s_m + 4 * lane);
-        x.a = tab_addr - 0x4B000000u;
         // ---- half A: keys 0-63, P over S columns 0-31
         l += wfa ? row_half_p<false>(s_col, mk, 0, k0, row_end, x) : row_half_p<true>(s_col, mk, 0, k0, row_end, x);
         tc::st_wait();
@@ -949,7 +922,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       if (!mbar_wait_warp(&sm.o_full[t], oc & 1, abort, p.err)) break;
       ++oc;
       tc::fence_after_sync();
-      const float vs = (p.v_scale_mode == 0) ? __ldg(p.v_scale) : __ldg(p.v_scale + (kv_of(p, bh) % p.v_scale_numel));
+      const float vs = u.vs;
       const float scale = 256.f * vs * ((l > 1e-6f) ? 1.f / l : 1.f);
       if (p.o_dtype == HYPERION_DTYPE_BF16) {
         store_o_row<HYPERION_DTYPE_BF16>(p.o, o_base, o_col, scale, row_ok, p.o_align32);
