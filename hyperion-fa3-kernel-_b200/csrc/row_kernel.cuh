@@ -207,11 +207,9 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
             raise_error(p.err, HYPERION_DEVERR_BAD_BLOCK);
           }
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
-          mask |= __shfl_xor_sync(0xffffffffu, mask, o);
-        }
+        bytes = __reduce_add_sync(0xffffffffu, bytes);
+        mask = ((unsigned long long)__reduce_or_sync(0xffffffffu, (uint32_t)(mask >> 32)) << 32) |
+               __reduce_or_sync(0xffffffffu, (uint32_t)mask);
         if (lane == 0) {
           sm.hdr[s].nkeys = n;
           sm.hdr[s].mask = mask;

@@ -562,12 +562,11 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
               raise_error(p.err, HYPERION_DEVERR_BAD_BLOCK);
             }
           }
+          // One warp reduction per word (redux.sync), not a chain of shuffles: this
+          // warp's per-tile latency lies on the kernel's critical path.
+          bytes = __reduce_add_sync(0xffffffffu, bytes);
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {
-            bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
-#pragma unroll
-            for (int w = 0; w < 4; ++w) mk[w] |= __shfl_xor_sync(0xffffffffu, mk[w], o);
-          }
+          for (int w = 0; w < 4; ++w) mk[w] = __reduce_or_sync(0xffffffffu, mk[w]);
           if (lane == 0) {
 #pragma unroll
             for (int w = 0; w < 4; ++w) sm.raw_mask[r][w] = mk[w];
