@@ -521,6 +521,13 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
   } else if (warp == kLoadWarp) {
     // ================================================================ loader
     const uint64_t pol = policy_evict_last();
+    // Pages of a tile by shifts when the page size is a power of two (every paged
+    // pool in practice, and the contiguous layout of a power-of-two context): an
+    // integer division by a run-time value costs this warp's per-tile chain, which
+    // bounds the kernel, a few dozen cycles.
+    const int bs = p.block_size;
+    const bool bs_pow2 = (bs & (bs - 1)) == 0;
+    const int bs_shift = __ffs(bs) - 1;
     uint32_t uc = 0, rit = 0;
     bool stop = false;
     while (!stop) {
@@ -542,9 +549,8 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           }
           const int k0 = j * kKeys;
           const int n = min(kKeys, kv_len - k0);
-          const int bs = p.block_size;
-          const int p0 = k0 / bs;
-          const int np = (k0 + n - 1) / bs - p0 + 1;
+          const int p0 = bs_pow2 ? (k0 >> bs_shift) : k0 / bs;
+          const int np = (bs_pow2 ? ((k0 + n - 1) >> bs_shift) : (k0 + n - 1) / bs) - p0 + 1;
           uint32_t bytes = 0;
           uint32_t mk[4] = {0u, 0u, 0u, 0u};
           for (int i = lane; i < np; i += 32) {
