@@ -291,10 +291,10 @@ def run_e2e(hyperion, wk, o, args, barrier):
     the new token's Q rows, K and V (bf16 [batch, KV heads, D]), positions and context
     lengths, writes K and V into the cache (kv_cache_write), runs the forward and
     copies O out.
-    Prefill: a step copies in all of the forward's inputs and copies O out.  Steps
-    are pipelined: the inputs of step i+1 go in and the O of step i-1 comes out
-    while step i computes (copy streams, double buffers; forwards stay in order on
-    one stream, since they share the workspace)."""
+    Prefill: a step copies in all of the forward's inputs and copies O out.
+    In both, steps are pipelined: the inputs of step i+1 go in and the O of step i-1
+    comes out while step i computes (copy streams, double buffers; cache writes and
+    forwards stay in order on one stream, since they share the workspace)."""
     dev = o.device
     main = torch.cuda.current_stream(dev)
     if wk.seq_q == 1:
@@ -311,43 +311,68 @@ def run_e2e(hyperion, wk, o, args, barrier):
         }
         # The step's inputs sit in one pinned staging buffer (each at a 256-byte
         # offset) and go over PCIe in one copy into a device buffer that the
-        # kernels read through fixed views.
+        # kernels read through fixed views.  Two device buffers and two O buffers
+        # pipeline the steps as the prefill case does: the inputs of step i+1 go in
+        # and the O of step i-1 comes out while step i computes; the cache writes
+        # and forwards stay in order on one stream.
         offs, total = {}, 0
         for k_, t in host.items():
             offs[k_] = total
             total += (t.numel() * t.element_size() + 255) // 256 * 256
         stage_h = torch.zeros(total, dtype=torch.uint8).pin_memory()
-        stage_d = torch.empty(total, dtype=torch.uint8, device=dev)
-        dbuf = {}
         for k_, t in host.items():
             n = t.numel() * t.element_size()
             stage_h[offs[k_]: offs[k_] + n].copy_(t.contiguous().view(torch.uint8).reshape(-1))
-            dbuf[k_] = stage_d[offs[k_]: offs[k_] + n].view(t.dtype).view(t.shape)
-        o_host = torch.empty(o.shape, dtype=o.dtype).pin_memory()
-        sub = type(wk)(**{**wk.__dict__, "q": dbuf["q"], "ctx_lens": dbuf["ctx_lens"]})
+        stage_d = [torch.empty(total, dtype=torch.uint8, device=dev) for _ in range(2)]
+        dbufs = [{k_: stage_d[b][offs[k_]: offs[k_] + t.numel() * t.element_size()].view(t.dtype).view(t.shape)
+                  for k_, t in host.items()} for b in range(2)]
+        subs = [type(wk)(**{**wk.__dict__, "q": dbufs[b]["q"], "ctx_lens": dbufs[b]["ctx_lens"]}) for b in range(2)]
+        outs = [o, torch.empty_like(o)]
+        o_hosts = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for _ in range(2)]
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        in_done = [torch.cuda.Event() for _ in range(2)]
+        fwd_done = [torch.cuda.Event() for _ in range(2)]
+        out_done = [torch.cuda.Event() for _ in range(2)]
 
-        def step():
-            stage_d.copy_(stage_h, non_blocking=True)
-            hyperion.kv_cache_write(dbuf["k_new"], dbuf["v_new"], dbuf["seq_ids"], dbuf["positions"],
-                                    wk.block_tables, wk.block_size, wk.num_blocks, wk.v_scale, wk.k, wk.v)
-            call_forward(hyperion, sub, o, path=args.path)
-            o_host.copy_(o, non_blocking=True)
+        def issue(i):
+            b = i % 2
+            with torch.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(fwd_done[b])
+                stage_d[b].copy_(stage_h, non_blocking=True)
+                in_done[b].record(s_in)
+            main.wait_event(in_done[b])
+            if i >= 2:
+                main.wait_event(out_done[b])
+            d = dbufs[b]
+            hyperion.kv_cache_write(d["k_new"], d["v_new"], d["seq_ids"], d["positions"], wk.block_tables,
+                                    wk.block_size, wk.num_blocks, wk.v_scale, wk.k, wk.v)
+            call_forward(hyperion, subs[b], outs[b], path=args.path)
+            fwd_done[b].record(main)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(fwd_done[b])
+                o_hosts[b].copy_(outs[b], non_blocking=True)
+                out_done[b].record(s_out)
 
-        step()
+        for i in range(2):
+            issue(i)
         torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(main)
-        for _ in range(args.steps):
-            step()
+        s_in.wait_event(e0)
+        for i in range(args.steps):
+            issue(i)
+        main.wait_stream(s_out)
         e1.record(main)
         torch.cuda.synchronize()
         barrier()
         h2d = total
         mode = ("resident KV cache: per step one H2D copy of Q, the new token's K/V (bf16), positions and context "
-                "lengths from a pinned staging buffer; kv_cache_write; forward; D2H of O")
-        return e0.elapsed_time(e1), h2d, o_host.numel() * o_host.element_size(), mode
+                "lengths from a pinned staging buffer; kv_cache_write; forward; D2H of O; steps pipelined over two "
+                "copy streams")
+        return e0.elapsed_time(e1), h2d, o_hosts[0].numel() * o_hosts[0].element_size(), mode
 
     keys = ("worklist", "q", "k", "v", "v_scale", "ctx_lens", "block_tables")
     host = {k: getattr(wk, k).cpu().pin_memory() for k in keys}
