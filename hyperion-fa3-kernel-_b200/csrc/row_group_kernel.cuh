@@ -9,7 +9,7 @@
 // consumer warp scores and accumulates all queries of the run against each stage.
 // HBM traffic per query falls by the run length.  The per-(query, key) arithmetic
 // is the row kernel's (popcount score, the reference's clamped online softmax per
-// 16-key group, f16x2 products of the hardware FP8 decode with the exact redo for
+// 32-key group, f16x2 products of the hardware FP8 decode with the exact redo for
 // codes 0x7F / 0xFF), with the FP8 decode of a key shared by the run's queries.
 //
 // Each query keeps its own key range [0, kv_end), so a run may also hold rows of
