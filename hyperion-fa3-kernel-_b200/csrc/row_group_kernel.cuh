@@ -34,8 +34,7 @@ constexpr int kGKeysPerWarp = kKeysPerStage / kGWarps;  // 32
 constexpr int kGThreads = 32 * (1 + kGWarps);
 // KV ring depth: 2 stages, so that 10 CTAs (head_dim 128) or 5 (head_dim 256) fit
 // an SM's shared memory.
-template <int D>
-constexpr int group_stages() { return 2; }
+constexpr int kGroupStages = 2;
 
 template <int W>
 struct RunSlot {
@@ -57,7 +56,7 @@ struct GroupSmem {
   static constexpr int W = D / 32;
   static constexpr int kKBytes = kKeysPerStage * W * 4;
   static constexpr int kVBytes = kKeysPerStage * D;
-  static constexpr int NS = group_stages<D>();
+  static constexpr int NS = kGroupStages;
   alignas(128) uint8_t k[NS][kKBytes];
   alignas(128) uint8_t v[NS][kVBytes];
   StageHeader hdr[NS];
