@@ -61,9 +61,9 @@ struct GroupSmem {
   alignas(128) uint8_t v[NS][kVBytes];
   StageHeader hdr[NS];
   RunSlot<W> slot[2];
-  float merge_m[kGWarps];
-  float merge_l[kGWarps];
-  float merge_acc[kGWarps][D];
+  float merge_m[kGWarps][2];  // two queries of the run per merge round
+  float merge_l[kGWarps][2];
+  float merge_acc[kGWarps][2][D];
   alignas(16) uint32_t wbuf[kGWarps][kGroupMax][kGKeysPerWarp];  // f16x2 {w, w} per query and key
   alignas(8) uint64_t full[NS];
   alignas(8) uint64_t empty[NS];
@@ -484,44 +484,53 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
       const bool stop = aborted || (*abort != 0);
       const float vs_run = (p.v_scale_mode == 2) ? 1.f : v_scale_for(p, sl.bh0, 0);
 
-      // ---- merge the four warps' (m, l, acc), one query at a time ----
+      // ---- merge the consumer warps' (m, l, acc), two queries per round ----
 #pragma unroll
-      for (int j = 0; j < G; ++j) {
-        if (j < nq) {
-          const float l_warp = warp_sum(l[j]);
-          if (lane == 0) {
-            sm.merge_m[cw] = m[j];
-            sm.merge_l[cw] = l_warp;
+      for (int j0 = 0; j0 < G; j0 += 2) {
+        if (j0 < nq) {
+          const bool two = j0 + 1 < nq;  // the same in every thread
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            if (q == 0 || two) {
+              const float l_warp = warp_sum(l[j0 + q]);
+              if (lane == 0) {
+                sm.merge_m[cw][q] = m[j0 + q];
+                sm.merge_l[cw][q] = l_warp;
+              }
+#pragma unroll
+              for (int i = 0; i < DPL; ++i) sm.merge_acc[cw][q][lane * DPL + i] = acc[j0 + q][i];
+            }
           }
-#pragma unroll
-          for (int i = 0; i < DPL; ++i) sm.merge_acc[cw][lane * DPL + i] = acc[j][i];
           named_bar_sync(1, 32 * kGWarps);
-          float M = -INFINITY;
+          for (int q = 0; q < (two ? 2 : 1); ++q) {
+            const int j = j0 + q;
+            float M = -INFINITY;
 #pragma unroll
-          for (int w2 = 0; w2 < kGWarps; ++w2) M = fmaxf(M, sm.merge_m[w2]);
-          float f[kGWarps];
-          float L = 0.f;
+            for (int w2 = 0; w2 < kGWarps; ++w2) M = fmaxf(M, sm.merge_m[w2][q]);
+            float f[kGWarps];
+            float L = 0.f;
 #pragma unroll
-          for (int w2 = 0; w2 < kGWarps; ++w2) {
-            const float mw = sm.merge_m[w2];
-            f[w2] = (mw == -INFINITY) ? 0.f : exp_clamped(mw - M);
-            L += sm.merge_l[w2] * f[w2];
-          }
-          for (int d = cw * 32 + lane; d < D; d += 32 * kGWarps) {
-            float a = 0.f;
+            for (int w2 = 0; w2 < kGWarps; ++w2) {
+              const float mw = sm.merge_m[w2][q];
+              f[w2] = (mw == -INFINITY) ? 0.f : exp_clamped(mw - M);
+              L += sm.merge_l[w2][q] * f[w2];
+            }
+            for (int d = cw * 32 + lane; d < D; d += 32 * kGWarps) {
+              float a = 0.f;
 #pragma unroll
-            for (int w2 = 0; w2 < kGWarps; ++w2) a += sm.merge_acc[w2][d] * f[w2];
-            a *= vs_run;
-            if (stop) continue;
-            if (p.n_split == 1) {
-              const float inv_l = (L > 1e-6f) ? 1.f / L : 1.f;
-              store_out(p.o, p.o_dtype, (long long)sl.orow[j] * D + d, a * inv_l);
-            } else {
-              float* part = p.partials + ((long long)sl.item[j] * p.n_split + sl.split) * (2 + D);
-              part[2 + d] = a;
-              if (d == 0) {
-                part[0] = M;
-                part[1] = L;
+              for (int w2 = 0; w2 < kGWarps; ++w2) a += sm.merge_acc[w2][q][d] * f[w2];
+              a *= vs_run;
+              if (stop) continue;
+              if (p.n_split == 1) {
+                const float inv_l = (L > 1e-6f) ? 1.f / L : 1.f;
+                store_out(p.o, p.o_dtype, (long long)sl.orow[j] * D + d, a * inv_l);
+              } else {
+                float* part = p.partials + ((long long)sl.item[j] * p.n_split + sl.split) * (2 + D);
+                part[2 + d] = a;
+                if (d == 0) {
+                  part[0] = M;
+                  part[1] = L;
+                }
               }
             }
           }
