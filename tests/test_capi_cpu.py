@@ -98,3 +98,34 @@ def test_python_boundary_checks_kv_group(hyperion):
     with pytest.raises(RuntimeError, match="kv_group"):
         hyperion.hyperion_apex_kernel(t, 4, t, None, t, None, t.to(torch.uint8), torch.ones(1), t[0],
                                       None, torch.zeros(4, 128), 1, 128, 16, 16, 1, 0.088, False, kv_group=0)
+
+
+def test_ctypes_structs_match_the_c_header_layout(tmp_path):
+    """The ctypes mirrors of hyperion_extents and hyperion_options must have the C
+    header's field offsets and sizes; a C program compiled against the header
+    prints them."""
+    import shutil
+    import subprocess
+
+    from hyperion_b200 import _capi
+
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not found")
+    structs = {"hyperion_extents": _capi.Extents, "hyperion_options": _capi.Options}
+    lines = ['#include "hyperion_b200.h"', "#include <stdio.h>", "#include <stddef.h>", "int main(void) {"]
+    for cname, cls in structs.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in cls._fields_:
+            lines.append(f'  printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "abi.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "abi"
+    subprocess.run([gcc, "-std=c99", "-I", os.path.join(REPO, "include"), str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    got = {tuple(line.split()[:2]): int(line.split()[2]) for line in out if line.strip()}
+    for cname, cls in structs.items():
+        assert got[(cname, "size")] == ctypes.sizeof(cls), cname
+        for fname, _ in cls._fields_:
+            assert got[(cname, fname)] == getattr(cls, fname).offset, (cname, fname)
