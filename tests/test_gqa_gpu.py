@@ -68,7 +68,7 @@ def test_gqa_paged_decode(hyperion, oracle, num_splits):
 def test_gqa_equals_block_tables_repeated_per_query_head(hyperion, oracle):
     """The same problem given to the ungrouped kernel, every query head's block-table
     row pointing at its KV head's pages.  Both meet the bar against the oracle, and
-    they agree with each other to rounding: both kernels sum the same 16-key groups of
+    they agree with each other to rounding: both kernels sum the same 32-key groups of
     f16x2 products, so any difference comes from a different split of the keys."""
     wk = W.make_paged("gqa_eq", 3, 8, [100, 999, 3000], page=16, seed=53, o_dtype=torch.float32, kv_heads=2)
     o_g, err, _, _ = run(hyperion, wk, path="row", num_splits=2)
@@ -210,3 +210,21 @@ def test_gqa_paged_causal_prefill(hyperion, oracle, path):
     assert err == 0 and info["path"] == path
     check(oracle, wk, o)
     check(oracle, dense, o)
+
+
+@pytest.mark.parametrize("o_dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("path,S_q", [("row", 1), ("tile", 130)])
+def test_gqa_half_precision_outputs(hyperion, oracle, o_dtype, path, S_q):
+    """bf16 and f16 O (the engine's types) from the grouped row kernel and the tile path."""
+    wk = W.make_dense("gqa_o", 2, 8, S_q, 600, causal=(S_q > 1), scale_mode="head", o_dtype=o_dtype, seed=65,
+                      kv_heads=2)
+    dev = torch.device("cuda", 0)
+    g = wk.to(dev)
+    o = torch.zeros(g.n_bh * g.seq_q, g.head_dim, dtype=o_dtype, device=dev)
+    hyperion.read_device_errors(dev, clear=True)
+    hyperion.hyperion_apex_kernel(g.worklist, g.total_work, g.q, None, g.k, None, g.v, g.v_scale, g.ctx_lens,
+                                  g.block_tables, o, g.seq_q, g.head_dim, g.head_dim // 8, g.block_size,
+                                  g.num_blocks, g.inv_sqrt_d, g.causal, path=path, kv_group=wk.kv_group)
+    assert hyperion.last_call_info()["path"] == path
+    assert hyperion.read_device_errors(dev, clear=True) == 0
+    check(oracle, wk, o.float().cpu().numpy())
