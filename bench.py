@@ -2,17 +2,21 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
                     [--workload prefill|decode|paged_decode|longctx|cpu_ref|decode_gqa|paged_decode_gqa]
-                    [--impl ours|reference] [--path auto|row|tile] [--gather]
+                    [--impl ours|reference] [--path auto|row|tile] [--no-sub]
 
 For N > 1 launch with torchrun (one rank per GPU, NCCL):
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
         --master-port P bench.py --gpus N --steps K --warmup W
 
 One step = one forward call (`hyperion_apex_kernel`) over one batch of the
-workload, inputs already in HBM.  Default workload: the causal prefill
+workload, inputs already in HBM.  The headline workload is the causal prefill
 B4 H32 S_q=S_kv=4096 D128, bf16 output, per GPU; at N GPUs each rank runs its own
-(batch, head) shard of a global batch of 4*N sequences (weak scaling: no data-path
-collective; --gather adds the output all-gather as a separate measurement).
+(batch, head) shard of a global batch of 4*N sequences (weak scaling, no
+data-path collective).  The same line carries sub-records, measured in the same
+run with the same method, for the decode workloads (whose metric is HBM GB/s)
+and the long-context prefill (B1 H64 S32768, heads split over the ranks:
+strong scaling).  At N > 1 every record also carries `with_gather`: the same
+steps with the all-gather of O (NCCL) inside each step.
 
 Timing: W untimed warm-up steps; L2 flushed (256 MiB write) before every timed
 step unless the inputs are larger than twice the L2; each step bracketed by CUDA
@@ -27,7 +31,9 @@ algorithm) on a bounded sample on this host's cores.
 
 `--impl reference` times the reference's own CPU path for this forward: the
 reference's kernel does not build and has no CPU attention, so that is the C
-restatement of its algorithm (oracle/), run on all host threads; rank 0 only.
+restatement of its algorithm (oracle/), run on all host threads, rank 0 only.
+Its inputs are built on the host and the CUDA library is never loaded; each
+step runs the oracle over the same fixed sample of (batch, head) rows.
 """
 from __future__ import annotations
 
@@ -39,16 +45,21 @@ import statistics
 import subprocess
 import sys
 import time
+import types
 
 REPO = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, os.path.join(REPO, "hyperion-fa3-kernel-_b200"))
+PKG_DIR = os.path.join(REPO, "hyperion-fa3-kernel-_b200")
+sys.path.insert(0, PKG_DIR)
 sys.path.insert(0, REPO)
 
 import torch  # noqa: E402
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# B200 datasheet figures: HGX HBM3e bandwidth and dense bf16 tensor throughput.
+SPEC_PEAKS = {"hbm_gbs": 7700.0, "bf16_tflops": 2250.0}
 METRIC = "attn Q·KV-token pairs/s"
 L2_BYTES = 126 << 20
+SUB_WORKLOADS = ("decode", "paged_decode", "decode_gqa", "longctx")
 
 
 def peaks():
@@ -65,6 +76,16 @@ def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return rank, world, local
+
+
+def host_only_package():
+    """Makes `hyperion_b200.workloads` / `.sharding` importable without running the
+    package's __init__, which loads the CUDA library: the reference arm builds its
+    inputs with them and must not load any of this repository's device code."""
+    if "hyperion_b200" not in sys.modules:
+        pkg = types.ModuleType("hyperion_b200")
+        pkg.__path__ = [os.path.join(PKG_DIR, "hyperion_b200")]
+        sys.modules["hyperion_b200"] = pkg
 
 
 # ---------------------------------------------------------------------------- clocks
@@ -122,6 +143,7 @@ class ClockSampler:
 
 # ---------------------------------------------------------------------------- workloads
 def build_workload(name, rank, world, device):
+    """The workload of `name` on this rank, its description and its scaling mode."""
     from hyperion_b200 import workloads as W
     from hyperion_b200.sharding import head_range
 
@@ -143,6 +165,27 @@ def build_workload(name, rank, world, device):
     return wk, desc, "weak"
 
 
+def input_bytes(wk):
+    return sum(t.numel() * t.element_size() for t in (wk.q, wk.k, wk.v, wk.block_tables))
+
+
+def workload_config(wk, desc, world, scaling):
+    """The `config` object of a JSON line: a function of the workload and the world
+    size only, so both arms of the benchmark print the same one."""
+    l2 = ("flushed before every timed step (256 MiB write)" if input_bytes(wk) <= 2 * L2_BYTES else
+          f"not flushed: inputs of {input_bytes(wk) / 1e9:.2f} GB are larger than L2")
+    return {
+        "workload": desc,
+        "global_batch": wk.batch * world if scaling == "weak" else wk.batch,
+        "heads": wk.heads if scaling == "weak" else wk.heads * world,
+        "seq_len": wk.seq_q if wk.seq_q > 1 else int(wk.ctx_lens.max()),
+        "head_dim": wk.head_dim,
+        "causal": wk.causal,
+        "parallelism": f"(batch, head) shards x{world}, no data-path collective",
+        "l2": l2,
+    }
+
+
 def call_forward(hyperion, wk, o, path="auto", **kw):
     hyperion.hyperion_apex_kernel(wk.worklist, wk.total_work, wk.q, None, wk.k, None, wk.v, wk.v_scale, wk.ctx_lens,
                                   wk.block_tables, o, wk.seq_q, wk.head_dim, wk.head_dim // 8, wk.block_size,
@@ -150,7 +193,8 @@ def call_forward(hyperion, wk, o, path="auto", **kw):
 
 
 def roofline_numbers(wk, pairs, kernel_ms, pk):
-    """Dominant kernel: algorithmic work per launch / average launch time."""
+    """Dominant kernel: algorithmic work per launch / average launch time, as a
+    fraction of the measured peak and of the datasheet peak."""
     if wk.seq_q == 1:
         # decode: K (D/8 B) + V (D B) per distinct (KV row, key) pair, plus Q rows and
         # O rows.  Without grouped-query heads every pair has its own KV row.
@@ -158,11 +202,13 @@ def roofline_numbers(wk, pairs, kernel_ms, pk):
             + wk.total_work * wk.head_dim * torch.tensor([], dtype=wk.o_dtype).element_size()
         achieved = nbytes / (kernel_ms * 1e-3) / 1e9
         return {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / pk["hbm_gbs"], "algorithmic_bytes_per_launch": nbytes}
+                "frac": achieved / pk["hbm_gbs"], "spec_peak": SPEC_PEAKS["hbm_gbs"],
+                "frac_of_spec": achieved / SPEC_PEAKS["hbm_gbs"], "algorithmic_bytes_per_launch": nbytes}
     flops = 2.0 * 2.0 * wk.head_dim * pairs  # QK (2D) + PV (2D) per pair
     achieved = flops / (kernel_ms * 1e-3) / 1e12
     return {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-            "frac": achieved / pk["bf16_tflops"], "algorithmic_flops_per_launch": flops}
+            "frac": achieved / pk["bf16_tflops"], "spec_peak": SPEC_PEAKS["bf16_tflops"],
+            "frac_of_spec": achieved / SPEC_PEAKS["bf16_tflops"], "algorithmic_flops_per_launch": flops}
 
 
 def read_traffic(kernel_tag):
@@ -182,17 +228,26 @@ def read_traffic(kernel_tag):
 
 
 # ---------------------------------------------------------------------------- CPU baseline
+def _sample_rows(wk, n_rows):
+    """The first n_rows of a seeded permutation of the workload's (batch, head) rows."""
+    order = torch.randperm(wk.n_bh, generator=torch.Generator().manual_seed(0)).tolist()
+    return order[:max(1, min(n_rows, wk.n_bh))]
+
+
+def _rows_per_call(wk, threads):
+    """Rows per oracle call: enough work items to keep every host thread busy."""
+    return max(1, (4 * threads + wk.seq_q - 1) // wk.seq_q)
+
+
 def cpu_baseline(wk_gpu, budget_s=12.0):
     """Times the C oracle on a sample of this workload's (batch, head) rows on all host
     threads.  Returns (pairs/s, threads, description)."""
     from oracle import oracle as O
-    from hyperion_b200 import workloads as W
 
     threads = O.lib().oracle_max_threads()
     n_bh = wk_gpu.n_bh
     bh_order = torch.randperm(n_bh, generator=torch.Generator().manual_seed(0)).tolist()
-    # Rows per oracle call: enough work items to keep every host thread busy.
-    per_call = max(1, (4 * threads + wk_gpu.seq_q - 1) // wk_gpu.seq_q)
+    per_call = _rows_per_call(wk_gpu, threads)
     done_pairs, spent, used = 0, 0.0, 0
     pos = 0
     # A workload shorter than the budget is timed again from its first row.
@@ -216,7 +271,7 @@ def cpu_baseline(wk_gpu, budget_s=12.0):
 
 def _subset_rows(wk, rows):
     """The listed (batch, head) rows of a workload, with every query row of each, as a
-    contiguous CPU workload (their keys gathered from the pool on the device)."""
+    contiguous CPU workload (their keys gathered from the pool where it lies)."""
     from hyperion_b200 import workloads as W
 
     cap = wk.num_blocks * wk.block_size
@@ -251,37 +306,65 @@ def _subset_rows(wk, rows):
                       heads=len(rows), inv_sqrt_d=wk.inv_sqrt_d)
 
 
-# ---------------------------------------------------------------------------- arms
+# ---------------------------------------------------------------------------- reference arm
 def run_reference(args):
-    rank, world, local = dist_env()
+    """The reference's CPU path on this host's cores: rank 0 alone, no GPU.
+
+    A step is one pass of the C restatement of the reference's per-item loop
+    (hyperion_fa3_production_final.py:338-593, oracle/hyperion_oracle.c) over a fixed
+    sample of the workload's (batch, head) rows with all their query rows, on all host
+    threads.  The sample is sized in the first warm-up step so that W + K steps take
+    about a minute and a half; every timed step runs the same sample, and the line's
+    ms_per_step is the measured time of those steps."""
+    rank, world, _ = dist_env()
     if rank != 0:
         return 0
+    host_only_package()
     from oracle import oracle as O
 
-    dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
-    wk, desc, _ = build_workload(args.workload, 0, 1, dev)
+    wk, desc, scaling = build_workload(args.workload, 0, world, torch.device("cpu"))
+    config = workload_config(wk, desc, world, scaling)
     threads = O.lib().oracle_max_threads()
-    budget = max(2.0, 150.0 / max(1, args.steps + args.warmup))
-    vals = []
+    per_call = _rows_per_call(wk, threads)
+    target_s = min(3.0, max(0.3, 90.0 / (args.warmup + args.steps)))
+    # Calibration: one call's worth of rows.
+    probe = _subset_rows(wk, _sample_rows(wk, per_call))
+    t0 = time.perf_counter()
+    O.forward_workload_c(probe, nthreads=threads)
+    t_probe = max(time.perf_counter() - t0, 1e-4)
+    n_calls = max(1, min(int(target_s / t_probe), (wk.n_bh + per_call - 1) // per_call))
+    rows = _sample_rows(wk, n_calls * per_call)
+    calls = [_subset_rows(wk, rows[i:i + per_call]) for i in range(0, len(rows), per_call)]
+    sample_pairs = sum(c.pairs() for c in calls)
+    step_s = []
     for i in range(args.warmup + args.steps):
-        v, threads, sample = cpu_baseline(wk, budget_s=budget)
+        t0 = time.perf_counter()
+        for c in calls:
+            O.forward_workload_c(c, nthreads=threads)
         if i >= args.warmup:
-            vals.append(v)
-    value = statistics.median(vals)
+            step_s.append(time.perf_counter() - t0)
+    total_s = sum(step_s)
+    value = sample_pairs * len(step_s) / total_s
+    sample = (f"{len(rows)} of {wk.n_bh} (batch, head) rows of this workload with all their query rows "
+              f"({sample_pairs} pairs, seeded choice), {per_call} rows per oracle call, the same rows every step")
     out = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "pairs/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": wk.pairs() / value * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": desc},
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "pairs/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_s / len(step_s) * 1e3,
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded random sign bits for Q/K, N(0,1) V as FP8 e4m3 with per-head scale",
+        "config": config, "pairs_per_step": sample_pairs,
         "cpu_baseline": {"value": value, "unit": "pairs/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "pairs/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
         "note": "the reference's CUDA kernel does not build and it has no CPU attention path; this is the C "
-                "restatement of its algorithm (oracle/hyperion_oracle.c) on all host threads",
+                "restatement of its algorithm (oracle/hyperion_oracle.c) on all host threads, inputs built on "
+                "the host",
     }
     print(json.dumps(out))
     return 0
 
 
+# ---------------------------------------------------------------------------- our arm
 def run_e2e(hyperion, wk, o, args, barrier):
     """Times args.steps steps through the public Python API with pinned host buffers;
     returns (total ms, H2D bytes per step, D2H bytes per step, description).
@@ -422,29 +505,17 @@ def run_e2e(hyperion, wk, o, args, barrier):
     return e0.elapsed_time(e1), h2d, o_hosts[0].numel() * o_hosts[0].element_size(), mode
 
 
-def run_ours(args):
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    pg = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-        pg = dist
-    import hyperion_b200 as hyperion
-
-    wk, desc, scaling = build_workload(args.workload, rank, world, dev)
+def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
+    """One workload on every rank: warm-up, a sustained run under the clock sampler,
+    args.steps timed steps, the e2e steps and, at N > 1, the steps with the output
+    gather.  Every rank takes the same collectives in the same order.  Returns the
+    JSON record on rank 0 and None elsewhere."""
+    wk, desc, scaling = build_workload(name, rank, world, dev)
     o = wk.new_output()
     pairs = wk.pairs()
     # Between timed steps: inputs larger than twice the L2 (126 MB) are streamed
     # from HBM anyway; smaller ones are evicted by a 256 MiB write before each step.
-    in_bytes = sum(t.numel() * t.element_size() for t in (wk.q, wk.k, wk.v, wk.block_tables))
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if in_bytes <= 2 * L2_BYTES else None
-    l2_note = (f"flushed before every timed step (256 MiB write)" if flush is not None else
-               f"not flushed: inputs of {in_bytes / 1e9:.2f} GB are larger than L2")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if input_bytes(wk) <= 2 * L2_BYTES else None
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
@@ -460,7 +531,7 @@ def run_ours(args):
     # nvidia-smi samples every 200 ms, longer than a short timed region: the sampler
     # starts before a >= 1.5 s sustained run of the same step that leads straight
     # into the timed steps, and stops after them.
-    clocks = ClockSampler([local] if world == 1 else list(range(world)))
+    clocks = ClockSampler([dev.index] if world == 1 else list(range(world)))
     if rank == 0:
         clocks.start()
     t_end = time.perf_counter() + 1.5
@@ -491,21 +562,30 @@ def run_ours(args):
     # e2e through the public API with pinned host buffers.
     e2e_ms, h2d, d2h, e2e_mode = run_e2e(hyperion, wk, o, args, barrier)
 
-    gather_ms = None
-    if args.gather and world > 1:
+    # N > 1: the same steps with the all-gather of O (NCCL) inside each step, for a
+    # caller that wants the whole output on every rank.
+    gather_total = 0.0
+    if world > 1:
         out_all = torch.empty((world,) + tuple(o.shape), dtype=o.dtype, device=dev)
         pg.all_gather_into_tensor(out_all, o)
         torch.cuda.synchronize()
-        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g_st = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        g_en = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         barrier()
-        g0.record(stream)
-        for _ in range(args.steps):
-            pg.all_gather_into_tensor(out_all, o)
-        g1.record(stream)
         torch.cuda.synchronize()
-        gather_ms = g0.elapsed_time(g1) / args.steps
+        for i in range(args.steps):
+            if flush is not None:
+                flush.fill_(i & 0xFF)
+            g_st[i].record(stream)
+            call_forward(hyperion, wk, o, path=args.path)
+            pg.all_gather_into_tensor(out_all, o)
+            g_en[i].record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        gather_total = sum(s.elapsed_time(e) for s, e in zip(g_st, g_en))
+        del out_all
 
-    vals = torch.tensor([total_ms, e2e_ms, float(pairs), gather_ms or 0.0], dtype=torch.float64, device=dev)
+    vals = torch.tensor([total_ms, e2e_ms, float(pairs), gather_total], dtype=torch.float64, device=dev)
     if pg is not None:
         mx = vals.clone()
         pg.all_reduce(mx, op=pg.ReduceOp.MAX)
@@ -514,44 +594,37 @@ def run_ours(args):
         total_ms_max, e2e_ms_max, gather_max = float(mx[0]), float(mx[1]), float(mx[3])
         pairs_all = float(sm[2])
     else:
-        total_ms_max, e2e_ms_max, gather_max = total_ms, e2e_ms, gather_ms or 0.0
+        total_ms_max, e2e_ms_max, gather_max = total_ms, e2e_ms, 0.0
         pairs_all = float(pairs)
 
+    rec = None
     if rank == 0:
         pk, pk_src = peaks()
         kernel_ms = total_ms / args.steps
         roof = roofline_numbers(wk, pairs, kernel_ms, pk)
         roof["peak_source"] = pk_src
-        kernel_tag = f"{info['path'] or 'row'}_kernel_{args.workload}"
         roof["kernel"] = f"{info['path']} kernel"
+        kernel_tag = f"{info['path'] or 'row'}_kernel_{name}"
         roof["traffic"] = read_traffic(kernel_tag)
-        if world == 1 and not args.no_cpu_baseline:
-            v_cpu, cores, sample = cpu_baseline(wk)
+        roof["traffic_source"] = (f"carried over from one ncu capture (profiles/{kernel_tag}.md), not measured in "
+                                  "this run" if roof["traffic"] is not None else None)
+        if world == 1 and cpu_budget_s > 0:
+            v_cpu, cores, sample = cpu_baseline(wk, budget_s=cpu_budget_s)
             cpu = {"value": v_cpu, "unit": "pairs/s", "cores": cores, "kind": "port", "sample": sample}
         else:
             cpu = None
         value = pairs_all * args.steps / (total_ms_max * 1e-3)
         e2e_val = pairs_all * args.steps / (e2e_ms_max * 1e-3)
-        c = {
-            "workload": desc,
-            "global_batch": wk.batch * world if scaling == "weak" else wk.batch,
-            "heads": wk.heads if scaling == "weak" else wk.heads * world,
-            "seq_len": wk.seq_q if wk.seq_q > 1 else int(wk.ctx_lens.max()),
-            "head_dim": wk.head_dim,
-            "causal": wk.causal,
-            "parallelism": f"(batch, head) shards x{world}, no data-path collective",
-            "l2": l2_note,
-            "path": info["path"],
-            "kv_splits": info["splits"],
-        }
-        out = {
+        rec = {
             "metric": METRIC, "value": value, "unit": "pairs/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms_max / args.steps, "higher_is_better": True,
             "scaling": scaling, "vs_baseline": None,
             "dtype": "sign-bit QK (e4m3 +-1 MMA, exact int) / f16 PV" if info["path"] == "tile"
                      else "sign-bit QK (popc, exact int) / f16x2 PV products, f32 accumulation",
             "data": "synthetic: seeded random sign bits for Q/K, N(0,1) V as FP8 e4m3 with per-head scale",
-            "config": c, "pairs_per_step": pairs_all,
+            "config": workload_config(wk, desc, world, scaling),
+            "launch": {"path": info["path"], "kv_splits": info["splits"], "grid": info["grid"]},
+            "pairs_per_step": pairs_all,
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": "pairs/s", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world, "mode": e2e_mode},
@@ -559,8 +632,44 @@ def run_ours(args):
             "clocks": clk, "device_errors": errs,
             "step_ms_min": min(step_ms), "step_ms_max": max(step_ms),
         }
-        if gather_ms is not None:
-            out["gather_ms"] = gather_max
+        if roof["bound"] == "hbm":
+            rec["hbm_gbs"] = roof["achieved"]
+        if world > 1:
+            rec["with_gather"] = {
+                "value": pairs_all * args.steps / (gather_max * 1e-3), "unit": "pairs/s",
+                "ms_per_step": gather_max / args.steps,
+                "gather_bytes_per_rank": o.numel() * o.element_size() * world,
+                "mode": "forward + NCCL all_gather_into_tensor of O in every step, max over ranks",
+            }
+    del wk, o, flush
+    torch.cuda.empty_cache()
+    return rec
+
+
+def run_ours(args):
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+    import hyperion_b200 as hyperion
+
+    out = measure(hyperion, args.workload, args, rank, world, dev, pg, 12.0 if not args.no_cpu_baseline else 0)
+    if args.workload == "prefill" and not args.no_sub:
+        subs = {}
+        for name in SUB_WORKLOADS:
+            rec = measure(hyperion, name, args, rank, world, dev, pg, 6.0 if not args.no_cpu_baseline else 0)
+            if rank == 0:
+                subs[name] = rec
+        if rank == 0:
+            out["sub"] = subs
+    if rank == 0:
         print(json.dumps(out))
     if pg is not None:
         pg.destroy_process_group()
@@ -577,7 +686,7 @@ def main():
                              "paged_decode_gqa"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--path", default="auto", choices=["auto", "row", "tile"])
-    ap.add_argument("--gather", action="store_true", help="also time the NCCL all-gather of O (N > 1)")
+    ap.add_argument("--no-sub", action="store_true", help="the headline workload only, without sub-records")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -181,9 +181,10 @@ int hyperion_launch_info(int32_t* out, int32_t n) {
   const DevInfo* di = nullptr;
   const int rc = get_dev(&di);
   if (rc) return rc;
-  const int32_t v[7] = {di->n_sm, di->row_ctas_128, di->row_smem_128, di->tile_ctas, di->tile_smem,
-                        di->row_ctas_256, di->tile_ok ? 1 : 0};
-  for (int i = 0; i < n && i < 7; ++i) out[i] = v[i];
+  const int32_t v[12] = {di->n_sm,           di->row_ctas_128,      di->row_smem_128,  di->tile_ctas,
+                         di->tile_smem,       di->row_ctas_256,      di->tile_ok ? 1 : 0, hyp::row::kThreads,
+                         hyp::row::kGThreads, di->group_ctas_128,    di->group_smem_128, hyp::tile::kThreads};
+  for (int i = 0; i < n && i < 12; ++i) out[i] = v[i];
   if (!di->tile_ok) g_last_error = "tile kernel unavailable: " + di->tile_why;
   return HYPERION_OK;
 }
@@ -206,6 +207,12 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   if (block_size < 1) return fail(HYPERION_ERR_INVALID_ARG, "block_size < 1");
   if (num_blocks < 1) return fail(HYPERION_ERR_INVALID_ARG, "num_blocks < 1");
   if (!std::isfinite(inv_sqrt_d)) return fail(HYPERION_ERR_INVALID_ARG, "inv_sqrt_d is not finite");
+  if (total_work == 0) {
+    // Nothing to do, whatever the tensors hold: a rank that owns no (batch, head)
+    // row passes empty ones.
+    g_last_call[0] = g_last_call[1] = g_last_call[2] = g_last_call[3] = 0;
+    return HYPERION_OK;
+  }
   if (ext->n_bh < 1) return fail(HYPERION_ERR_INVALID_ARG, "n_bh (context_lens numel) < 1");
   if (ext->pool_rows < 1) return fail(HYPERION_ERR_INVALID_ARG, "pool_rows < 1");
   if (ext->v_scale_numel < 1) return fail(HYPERION_ERR_INVALID_ARG, "V_scale is empty");
@@ -224,10 +231,6 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   if (workspace == nullptr) return fail(HYPERION_ERR_WORKSPACE, "workspace is NULL");
   if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
     return fail(HYPERION_ERR_WORKSPACE, "workspace must be 256-byte aligned");
-  if (total_work == 0) {
-    g_last_call[0] = g_last_call[1] = g_last_call[2] = g_last_call[3] = 0;
-    return HYPERION_OK;
-  }
   if (!worklist || !Q || !K_cache || !V_cache || !V_scale || !context_lens || !O)
     return fail(HYPERION_ERR_INVALID_ARG, "a tensor pointer is NULL");
   if (reinterpret_cast<uintptr_t>(worklist) % 16 != 0)
@@ -296,10 +299,12 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
                 ("tile path needs head_dim 128, a per-tensor or per-head V scale and a device that loaded it" +
                  (di->tile_ok ? std::string() : "; " + di->tile_why)).c_str());
 
-  cudaError_t e = cudaMemsetAsync(ws + hyp::kWsCounters, 0, 64, st);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(counters)");
-
+  // The work counters are zeroed on the stream just before the kernels, once every
+  // check has passed: a refused call leaves the workspace untouched.
+  cudaError_t e = cudaSuccess;
   if (path == HYPERION_PATH_TILE) {
+    e = cudaMemsetAsync(ws + hyp::kWsCounters, 0, 64, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(counters)");
     int grid = 0;
     rc = hyp::tile::launch(p, di->n_sm, di->tile_ctas, di->tile_smem, st, &grid);
     if (rc) return rc;
@@ -327,10 +332,12 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   p.n_split = ns;
   const long long units = (long long)total_work * ns;
   if (units > 0x7fffffffLL) return fail(HYPERION_ERR_UNSUPPORTED, "too many work units");
+  if (grouped && chunks * ns > 0x7fffffffLL) return fail(HYPERION_ERR_UNSUPPORTED, "too many work units");
+  e = cudaMemsetAsync(ws + hyp::kWsCounters, 0, 64, st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(counters)");
   int grid = 0;
   if (grouped) {
     const long long gunits = chunks * ns;
-    if (gunits > 0x7fffffffLL) return fail(HYPERION_ERR_UNSUPPORTED, "too many work units");
     const int ctas = (head_dim == 256) ? di->group_ctas_256 : di->group_ctas_128;
     const int smem = (head_dim == 256) ? di->group_smem_256 : di->group_smem_128;
     grid = (int)std::min<long long>(gunits, (long long)di->n_sm * ctas);

@@ -6,7 +6,8 @@
 // The format is the one the forward reads (README.md:18-23):
 //   K: bit d%32 of word d/32 of the key's row is 1 where k[d] >= 0;
 //   V: code = e4m3(clamp(v / scale, -448, 448)), rounded to nearest even, where the
-//      scale is V_scale[0] (numel 1) or V_scale[bh % numel] (per head / per (b, h)).
+//      scale is V_scale[0] (numel 1), V_scale[slot] (numel == pool rows, the
+//      reference's per-slot layout) or V_scale[bh % numel] (per head / per (b, h)).
 // Slot of token t of sequence b, head h (bh = b*H + h): page = t / block_size,
 // id = block_tables[bh, page] (or bh*num_blocks + page with no table), slot =
 // id*block_size + t%block_size -- the same addressing as the forward
@@ -84,7 +85,10 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) kv_write_kernel(Args a) {
     if (lane == 0) raise_error(a.err, HYPERION_DEVERR_BAD_BLOCK);
     return;
   }
-  const float scale = __ldg(a.v_scale + (a.v_scale_numel == 1 ? 0 : bh % a.v_scale_numel));
+  // The forward's rule for the scale a code is decoded with: per tensor (numel 1),
+  // per slot (numel == pool rows), else per head / per (batch, head).
+  const long long si = a.v_scale_numel == 1 ? 0 : (a.v_scale_numel == a.pool_rows ? slot : bh % a.v_scale_numel);
+  const float scale = __ldg(a.v_scale + si);
   const T* kr = static_cast<const T*>(a.k_new) + wid * D;
   const T* vr = static_cast<const T*>(a.v_new) + wid * D;
   uint32_t word = 0;

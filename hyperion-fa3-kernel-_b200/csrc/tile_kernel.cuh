@@ -86,9 +86,6 @@ struct Smem {
   alignas(128) uint8_t raw_k[kRawStages][kKeys * 16];
   alignas(128) uint8_t raw_v[kRawStages][kKeys * 128];
   uint32_t raw_mask[kRawStages][4];
-  // Softmax weights by table: entry j (one copy per lane, so a warp's lookups never
-  // share a bank) holds exp(max(|c| * 2(j - 128), -80)), the weight of a score that
-  // lies 2(j - 128) above the row's running integer maximum (|c| = |inv_sqrt_d|).
   uint32_t kv_mask[kKvStages][4];
   UnitInfo unit[2];
   alignas(8) uint64_t sched_full[2];

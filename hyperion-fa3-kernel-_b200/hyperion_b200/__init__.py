@@ -27,7 +27,9 @@ Differences from the reference's boundary, all forced by the sign-bit path:
   * a block_tables tensor with numel 0 selects the contiguous KV layout.
 Errors in arguments raise RuntimeError (the reference's TORCH_CHECK would);
 errors found on the device (bad block ids, out-of-range work items) are
-accumulated in a per-device error word: `read_device_errors()`.
+accumulated in the error word of the calling stream's workspace:
+`read_device_errors()`.  Each (device, stream) has its own workspace, so forwards
+on different streams never share a work counter or split-KV partials.
 """
 from __future__ import annotations
 
@@ -60,16 +62,25 @@ _workspaces: dict = {}
 
 
 def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """Per-device workspace (work counter, error word, split-KV partials), grown on demand."""
+    """Workspace (work counter, error word, split-KV partials) of the current stream of
+    `device`, grown on demand.
+
+    One workspace per (device, stream): forwards on two streams then never share a
+    work counter or split-KV partials, and the calls that use one workspace are
+    ordered by its stream.  It is allocated on that stream as well, so when it grows
+    the caching allocator hands the old block out again only after the work already
+    queued on the stream."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
+    dev = torch.device("cuda", idx)
+    key = (idx, torch.cuda.current_stream(dev).cuda_stream)
     with _ws_lock:
-        ws = _workspaces.get(idx)
+        ws = _workspaces.get(key)
         if ws is None or ws.numel() < nbytes:
-            new = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=torch.device("cuda", idx))
+            new = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=dev)
             if ws is not None:
                 new[:256].copy_(ws[:256])  # keep the sticky error word
             ws = new
-            _workspaces[idx] = ws
+            _workspaces[key] = ws
         return ws
 
 
@@ -139,7 +150,9 @@ def hyperion_apex_kernel(
            "worklist must be int32 [n, 4]")
     _check(0 <= total_work <= worklist.size(0), "total_work must be in [0, worklist.size(0)]")
     _check(context_lens.dtype == torch.int32, "context_lens must be int32")
-    _check(V_scale.dtype == torch.float32 and V_scale.numel() >= 1, "V_scale must be a non-empty float32 tensor")
+    # An empty call (a rank that owns no (batch, head) row) may pass empty tensors.
+    _check(V_scale.dtype == torch.float32 and (V_scale.numel() >= 1 or total_work == 0),
+           "V_scale must be a non-empty float32 tensor")
     _check(V_cache.element_size() == 1, "V_cache must hold one byte per element (FP8 e4m3 codes)")
     _check(O.dtype in _O_DTYPES, "O must be float16, bfloat16 or float32")
     _check(O.is_contiguous(), "O must be contiguous")
@@ -208,7 +221,8 @@ def kv_cache_write(K_new: torch.Tensor, V_new: torch.Tensor, seq_ids: torch.Tens
     seq*n_heads + head, or the contiguous layout when block_tables is None / empty):
     K as sign bits into K_cache [pool_rows, head_dim/32] (int32 / uint32 storage), V
     as e4m3 codes of clamp(v / scale, -448, 448) into V_cache [pool_rows, head_dim]
-    uint8, scale V_scale[0] or V_scale[(seq*n_heads + head) % numel].  Rows whose
+    uint8, with the scale the forward decodes that slot with: V_scale[0] (numel 1),
+    V_scale[slot] (numel == pool rows) or V_scale[(seq*n_heads + head) % numel].  Rows whose
     position or page falls outside the pool are skipped and flagged
     (read_device_errors)."""
     dtypes = {torch.float16: _capi.DTYPE_F16, torch.bfloat16: _capi.DTYPE_BF16, torch.float32: _capi.DTYPE_F32}
@@ -246,8 +260,8 @@ def kv_cache_write(K_new: torch.Tensor, V_new: torch.Tensor, seq_ids: torch.Tens
 
 def hyperion_reset_counter(*, grid=None, block=None, device=None) -> None:
     """Reference call site hyperion_fa3_production_final.py:905.  Zeroes the work
-    counter of the current device's workspace on the current stream.  The forward
-    also zeroes it itself, so calling this is optional."""
+    counter of the workspace of the current stream of the current device, on that
+    stream.  The forward also zeroes it itself, so calling this is optional."""
     dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index)
     with torch.cuda.device(dev):
         ws = _workspace(dev, 1 << 16)
@@ -257,7 +271,9 @@ def hyperion_reset_counter(*, grid=None, block=None, device=None) -> None:
 
 
 def read_device_errors(device=None, clear: bool = True) -> int:
-    """Synchronises the current stream and returns the DEVERR_* flags raised on `device`."""
+    """Synchronises the current stream of `device` and returns the DEVERR_* flags that
+    the calls issued on that stream raised (each stream has its own workspace and so
+    its own error word)."""
     dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index)
     with torch.cuda.device(dev):
         ws = _workspace(dev, 1 << 16)
@@ -271,12 +287,13 @@ def read_device_errors(device=None, clear: bool = True) -> int:
 
 def launch_info() -> dict:
     """Launch facts derived from the current device (SM count, CTAs per SM, shared memory)."""
-    out = (ctypes.c_int32 * 7)()
-    rc = _capi.lib.hyperion_launch_info(out, 7)
+    keys = ("sm_count", "row_ctas_per_sm", "row_smem_bytes", "tile_ctas_per_sm", "tile_smem_bytes",
+            "row_ctas_per_sm_d256", "tile_available", "row_threads", "group_threads", "group_ctas_per_sm",
+            "group_smem_bytes", "tile_threads")
+    out = (ctypes.c_int32 * len(keys))()
+    rc = _capi.lib.hyperion_launch_info(out, len(keys))
     if rc != _capi.HYPERION_OK:
         raise RuntimeError(f"hyperion_launch_info failed: {_capi.last_error()}")
-    keys = ("sm_count", "row_ctas_per_sm", "row_smem_bytes", "tile_ctas_per_sm", "tile_smem_bytes",
-            "row_ctas_per_sm_d256", "tile_available")
     return dict(zip(keys, list(out)))
 
 

@@ -55,16 +55,25 @@ def build_worklist(q_lens: torch.Tensor, n_heads: int, kv_signatures: Optional[S
     return wl
 
 
-def launch_config(device=None) -> Tuple[Tuple[int, int, int], Tuple[int, int, int], int]:
-    """(grid, block, shared) of the library's main kernels on `device`: the row kernel's
-    resident CTAs and block size, and the tile kernel's shared memory."""
+def launch_config(device=None, seq_q: int = 1) -> Tuple[Tuple[int, int, int], Tuple[int, int, int], int]:
+    """(grid, block, shared) of the kernel the forward launches for `seq_q` query rows per
+    (batch, head), as the library sized it on `device`: the row kernel for decode
+    (seq_q 1), the tcgen05 tile kernel for prefill (seq_q >= 64) -- its resident
+    CTAs, its block size and its dynamic shared memory.  The forward treats the
+    triple it is given as a hint only."""
     from . import launch_info
 
     dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index)
     with torch.cuda.device(dev):
         info = launch_info()
-    grid = (info["sm_count"] * info["row_ctas_per_sm"], 1, 1)
-    return grid, (160, 1, 1), int(info["tile_smem_bytes"])
+    if seq_q >= 64 and info["tile_available"]:
+        return (info["sm_count"] * info["tile_ctas_per_sm"], 1, 1), (info["tile_threads"], 1, 1), \
+            int(info["tile_smem_bytes"])
+    if seq_q > 1:
+        return (info["sm_count"] * info["group_ctas_per_sm"], 1, 1), (info["group_threads"], 1, 1), \
+            int(info["group_smem_bytes"])
+    return (info["sm_count"] * info["row_ctas_per_sm"], 1, 1), (info["row_threads"], 1, 1), \
+        int(info["row_smem_bytes"])
 
 
 def memory_requirements(model_size_b: float, context_len: int, batch_size: int, num_layers: int, num_heads: int,

@@ -57,7 +57,10 @@ def shard_workload(wk: Workload, heads: range) -> Workload:
     rows = shard_bh(wk.batch, H, heads).to(dev)
     kv_rows = shard_bh(wk.batch, Hkv, kv_heads).to(dev)
     nb, nkv = len(rows), len(kv_rows)
-    q = wk.q.view(wk.n_bh, wk.seq_q, -1)[rows].reshape(nb * wk.seq_q, -1)
+    # Explicit row widths: a rank that owns no head (more ranks than KV heads) gets
+    # empty tensors of the right width.
+    qw, kw_, vw = wk.q.shape[-1], wk.k.shape[-1], wk.v.shape[-1]
+    q = wk.q.view(wk.n_bh, wk.seq_q, qw)[rows].reshape(nb * wk.seq_q, qw)
     ctx = wk.ctx_lens[kv_rows]
     vs = wk.v_scale
     pool_rows = wk.v.shape[0]
@@ -71,8 +74,8 @@ def shard_workload(wk: Workload, heads: range) -> Workload:
         k, v = wk.k, wk.v
     else:
         span = wk.num_blocks * wk.block_size
-        k = wk.k.view(wk.n_kv_bh, span, -1)[kv_rows].reshape(nkv * span, -1)
-        v = wk.v.view(wk.n_kv_bh, span, -1)[kv_rows].reshape(nkv * span, -1)
+        k = wk.k.view(wk.n_kv_bh, span, kw_)[kv_rows].reshape(nkv * span, kw_)
+        v = wk.v.view(wk.n_kv_bh, span, vw)[kv_rows].reshape(nkv * span, vw)
         if per_slot:
             vs = vs.view(wk.n_kv_bh, span)[kv_rows].reshape(-1)
         bt = wk.block_tables

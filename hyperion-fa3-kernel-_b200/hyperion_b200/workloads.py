@@ -62,12 +62,12 @@ class Workload:
     o_dtype: torch.dtype
     batch: int
     heads: int
-    inv_sqrt_d: float = 0.0
+    inv_sqrt_d: Optional[float] = None  # None: 1 / sqrt(head_dim); 0 gives flat weights
     meta: dict = field(default_factory=dict)
     kv_group: int = 1  # query heads per KV head; KV-side arrays are indexed by bh // kv_group
 
     def __post_init__(self):
-        if not self.inv_sqrt_d:
+        if self.inv_sqrt_d is None:
             self.inv_sqrt_d = 1.0 / math.sqrt(self.head_dim)
 
     @property

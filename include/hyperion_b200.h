@@ -153,9 +153,12 @@ int hyperion_reset_counter(void* workspace, size_t workspace_bytes, void* stream
 int hyperion_read_device_errors(void* workspace, size_t workspace_bytes, void* stream,
                                 uint32_t* flags, int32_t clear);
 
-/* Launch facts the library derived from the device: SM count, CTAs per SM of the
- * row kernel and of the tile kernel, and the dynamic shared memory of each.
- * Fills up to `n` int32 values of `out`; returns HYPERION_OK. */
+/* Launch facts the library derived from the device.  Fills up to `n` int32 values of
+ * `out` (returns HYPERION_OK):
+ *   [0] SM count            [1] row kernel CTAs per SM   [2] row kernel shared bytes
+ *   [3] tile kernel CTAs/SM [4] tile kernel shared bytes [5] row kernel CTAs per SM, head_dim 256
+ *   [6] tile kernel loaded  [7] row kernel threads       [8] grouped row kernel threads
+ *   [9] grouped row kernel CTAs per SM  [10] its shared bytes  [11] tile kernel threads */
 int hyperion_launch_info(int32_t* out, int32_t n);
 
 /* What the last forward on this thread did: out[0] = path (HYPERION_PATH_ROW or
@@ -179,7 +182,8 @@ int32_t hyperion_version(void);
  * contiguous slot bh*num_blocks*block_size + pos when block_tables_numel is 0).
  * K: sign bits (1 where k >= 0) into K_cache [pool_rows, head_dim/32] uint32;
  * V: e4m3 codes of clamp(v / scale, -448, 448), round to nearest even, into V_cache
- * [pool_rows, head_dim] uint8, with scale V_scale[0] (numel 1) or V_scale[bh % numel].
+ * [pool_rows, head_dim] uint8, with the scale the forward decodes that slot with:
+ * V_scale[0] (numel 1), V_scale[slot] (numel == pool_rows) or V_scale[bh % numel].
  * Positions or page ids outside the pool set HYPERION_DEVERR_BAD_ITEM / _BAD_BLOCK in
  * the workspace error word and that row is skipped.  Asynchronous on `stream`. */
 int hyperion_kv_cache_write(const void* K_new, const void* V_new, int32_t in_dtype,

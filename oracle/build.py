@@ -26,8 +26,17 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_DIR = os.path.join(HERE, "_ref")
 REF_SO = os.path.join(REF_DIR, "libref_fp8.so")
-REF_SRC = os.environ.get("HYPERION_REFERENCE_DIR", "/root/reference")
-REF_FILE = os.path.join(REF_SRC, "hyperion_fa3_production_final.py")
+REF_MODULE = "hyperion_fa3_production_final.py"
+
+
+def reference_file() -> str | None:
+    """The reference's module inside the checkout named by HYPERION_REFERENCE_DIR, or
+    None when the variable is unset or the file is absent (the GPU box has none)."""
+    root = os.environ.get("HYPERION_REFERENCE_DIR")
+    if not root:
+        return None
+    path = os.path.join(root, REF_MODULE)
+    return path if os.path.exists(path) else None
 
 CFLAGS = ["-O3", "-march=x86-64-v2", "-fPIC", "-shared", "-ffp-contract=off", "-std=gnu11", "-pthread"]
 
@@ -81,12 +90,13 @@ EXPORT = "\nfloat ref_fp8_e4m3_to_fp32(uint8_t x) { return fp8_e4m3_to_fp32(x); 
 
 def build_ref(force: bool = False) -> str | None:
     """Compiles the reference's FP8 decode; None when the reference is absent."""
-    if not os.path.exists(REF_FILE):
+    ref_file = reference_file()
+    if ref_file is None:
         return REF_SO if os.path.exists(REF_SO) else None
     if not force and os.path.exists(REF_SO) and os.path.getmtime(REF_SO) >= os.path.getmtime(__file__):
         return REF_SO
     os.makedirs(REF_DIR, exist_ok=True)
-    func = _cut_function(_reference_cuda_source(REF_FILE), "fp8_e4m3_to_fp32")
+    func = _cut_function(_reference_cuda_source(ref_file), "fp8_e4m3_to_fp32")
     cmd = [_cc(), "-O2", "-fPIC", "-shared", "-x", "c", "-", "-o", REF_SO + ".tmp", "-lm"]
     res = subprocess.run(cmd, input=SHIM + func + EXPORT, capture_output=True, text=True)
     if res.returncode != 0:

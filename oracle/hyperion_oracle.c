@@ -6,7 +6,7 @@
  *
  * Parity status: partially pinned.  The FP8 decode is checked code-for-code
  * against the reference's own fp8_e4m3_to_fp32 compiled from its source
- * (oracle/build_ref.py -> oracle/_ref); the reference ships no tests, golden
+ * (oracle/build.py, build_ref() -> oracle/_ref); the reference ships no tests, golden
  * vectors or runnable attention kernel (its CUDA source does not compile), so the
  * scoring and softmax below are restated from its source and README and pinned
  * only by hand-built known-answer cases.

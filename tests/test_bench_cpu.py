@@ -45,3 +45,30 @@ def test_cpu_baseline_sample_reproduces_its_rows(oracle, kv_heads):
     got, _, err, _ = oracle.forward_workload_c(sub)
     assert err == 0
     assert np.array_equal(got, full[rows])
+
+
+def test_reference_arm_inputs_load_no_device_code_of_this_repository():
+    """The reference arm builds its inputs with the workload generators but must not
+    map libhyperion_b200.so: it times the CPU restatement alone."""
+    import subprocess
+    import sys
+
+    code = ("import bench, torch; bench.host_only_package(); "
+            "wk, desc, sc = bench.build_workload('cpu_ref', 0, 1, torch.device('cpu')); "
+            "print(wk.pairs(), sorted(bench.workload_config(wk, desc, 1, sc))); "
+            "print('MAPPED' if 'libhyperion_b200' in open('/proc/self/maps').read() else 'CLEAN')")
+    res = subprocess.run([sys.executable, "-c", code], cwd=bench.REPO, capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stderr
+    assert res.stdout.strip().splitlines()[-1] == "CLEAN"
+    assert res.stdout.startswith(str(8 * 512 * 512))
+
+
+def test_config_is_the_same_for_a_workload_on_either_device():
+    """Both arms print workload_config(...) of the same workload; it must not depend on
+    where the tensors live or on anything a kernel launch reports."""
+    wk = W.make_dense("c", 2, 4, 64, 64, causal=True, o_dtype=torch.bfloat16)
+    a = bench.workload_config(wk, "desc", 2, "weak")
+    b = bench.workload_config(wk.to("cpu"), "desc", 2, "weak")
+    assert a == b
+    assert set(a) == {"workload", "global_batch", "heads", "seq_len", "head_dim", "causal", "parallelism", "l2"}
+    assert a["global_batch"] == 4 and a["seq_len"] == 64

@@ -129,3 +129,21 @@ def test_ctypes_structs_match_the_c_header_layout(tmp_path):
         assert got[(cname, "size")] == ctypes.sizeof(cls), cname
         for fname, _ in cls._fields_:
             assert got[(cname, fname)] == getattr(cls, fname).offset, (cname, fname)
+
+
+def test_c_boundary_accepts_an_empty_call_from_an_idle_rank(hyperion):
+    """A rank that owns no (batch, head) row (more ranks than KV heads) calls with
+    total_work 0 and empty tensors: nothing to launch, status OK, device untouched."""
+    from hyperion_b200 import _capi
+
+    ext = _capi.Extents(0, 0, 0, 0, _capi.DTYPE_BF16, 0, 0, 0)
+    rc = _capi.lib.hyperion_apex_kernel(None, 0, None, None, None, None, None, None, None, None, None, 1, 128, 16,
+                                        16, 1, ctypes.c_float(0.088), 1, ctypes.byref(ext), None, 0, None)
+    assert rc == _capi.HYPERION_OK
+    out = (ctypes.c_int32 * 4)()
+    _capi.lib.hyperion_last_call_info(out, 4)
+    assert list(out) == [0, 0, 0, 0]
+    # Scalar arguments are still checked.
+    rc = _capi.lib.hyperion_apex_kernel(None, 0, None, None, None, None, None, None, None, None, None, 1, 96, 12,
+                                        16, 1, ctypes.c_float(0.088), 1, ctypes.byref(ext), None, 0, None)
+    assert rc == _capi.HYPERION_ERR_UNSUPPORTED

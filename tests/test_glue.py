@@ -65,5 +65,21 @@ def test_device_worklist_drives_the_forward(hyperion, oracle):
     rows = (wl[:, 1].long() * g.seq_q + wl[:, 0].long()).cpu().numpy()
     ok, mx, mn = oracle.tolerance_check(o.cpu().numpy()[rows], ref[rows], 2e-2, 2e-3)
     assert ok, (mx, mn)
+    # The launch hints describe the kernel the forward really launched for this
+    # worklist (the tile kernel for 64+ query rows per (batch, head)).
+    info = hyperion.launch_info()
+    grid, block, shared = glue.launch_config(dev, seq_q=g.seq_q)
+    assert hyperion.last_call_info()["path"] == "tile"
+    assert block == (info["tile_threads"], 1, 1) == (512, 1, 1)
+    assert grid[0] == info["sm_count"] * info["tile_ctas_per_sm"] and shared == info["tile_smem_bytes"]
+    # Decode: the row kernel's 96-thread CTAs (a producer warp and two consumer warps).
     grid, block, shared = glue.launch_config(dev)
-    assert grid[0] >= 148 and block[0] > 0 and shared > 0
+    assert block == (info["row_threads"], 1, 1) == (96, 1, 1)
+    assert grid[0] == info["sm_count"] * info["row_ctas_per_sm"] >= 148 and shared == info["row_smem_bytes"] > 0
+    d = W.make_dense("lc_decode", 2, 2, 1, 300, o_dtype=torch.float32, seed=5).to(dev)
+    od = d.new_output()
+    hyperion.hyperion_apex_kernel(d.worklist, d.total_work, d.q, None, d.k, None, d.v, d.v_scale, d.ctx_lens,
+                                  d.block_tables, od, 1, 128, 16, d.block_size, d.num_blocks, d.inv_sqrt_d, False,
+                                  grid=grid, block=block, shared=shared)
+    assert hyperion.last_call_info()["path"] == "row"
+    assert hyperion.last_call_info()["grid"] <= grid[0]

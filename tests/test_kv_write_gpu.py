@@ -159,3 +159,53 @@ def test_written_cache_feeds_the_forward(hyperion, oracle):
     assert err == 0
     ok, mx, mn = oracle.tolerance_check(o.cpu().numpy(), ref, 2e-2, 2e-3)
     assert ok, (mx, mn)
+
+
+def test_per_slot_scale_is_the_one_the_forward_decodes_with(hyperion, oracle):
+    """The reference keeps one V scale per cache slot (V_scale[slot]).  The writer must
+    quantise each row with the scale of the slot it lands in, which is the one the
+    forward decodes it with; the round trip then matches the oracle and the codes match
+    the CPU quantiser with per-slot scales bit for bit."""
+    torch.manual_seed(13)
+    H, D, page = 2, 128, 16
+    lens = [70, 33]
+    bt, nb, pool_rows = _paged_layout(lens, H, page, seed=8)
+    seq, pos = _tokens(lens)
+    n = seq.numel()
+    dev = torch.device("cuda", 0)
+    k = torch.randn(n, H, D)
+    v = torch.randn(n, H, D) * torch.rand(n, H, 1) * 4
+    slot_scale = (torch.rand(pool_rows) * 0.02 + 0.002).float()
+    kc = torch.zeros(pool_rows, D // 32, dtype=torch.int32, device=dev)
+    vc = torch.full((pool_rows, D), SENTINEL, dtype=torch.uint8, device=dev)
+    hyperion.read_device_errors(dev, clear=True)
+    hyperion.kv_cache_write(k.to(dev), v.to(dev), seq.to(dev), pos.to(dev), bt.to(dev), page, nb,
+                            slot_scale.to(dev), kc, vc)
+    assert hyperion.read_device_errors(dev, clear=True) == 0
+    got = vc.cpu()
+    for i in range(n):
+        b, t = int(seq[i]), int(pos[i])
+        for h in range(H):
+            slot = int(bt[b * H + h, t // page]) * page + t % page
+            assert torch.equal(got[slot], W.fp8_quantize(v[i, h], slot_scale[slot]))
+    n_bh = len(lens) * H
+    q = W.sign_pack(torch.randn(n_bh, D)).to(dev)
+    ctx = torch.tensor([L for L in lens for _ in range(H)], dtype=torch.int32, device=dev)
+    wl = W.dense_worklist(n_bh, 1, dev)
+    wl[:, 0] = 0
+    wk = W.Workload(name="slot", worklist=wl, q=q, k=kc, v=vc, v_scale=slot_scale.to(dev), ctx_lens=ctx,
+                    block_tables=bt.to(dev), seq_q=1, head_dim=D, block_size=page, num_blocks=nb, causal=False,
+                    o_dtype=torch.float32, batch=len(lens), heads=H)
+    o = torch.zeros(n_bh, D, dtype=torch.float32, device=dev)
+    hyperion.hyperion_apex_kernel(wk.worklist, wk.total_work, wk.q, None, wk.k, None, wk.v, wk.v_scale, wk.ctx_lens,
+                                  wk.block_tables, o, 1, D, D // 8, page, nb, wk.inv_sqrt_d, False)
+    assert hyperion.read_device_errors(dev, clear=True) == 0
+    ref, _, err, _ = oracle.forward_workload_c(wk.to("cpu"))
+    assert err == 0
+    ok, mx, mn = oracle.tolerance_check(o.cpu().numpy(), ref, 2e-2, 2e-3)
+    assert ok, (mx, mn)
+    # The values the forward saw are the clamped V to within e4m3 rounding.
+    dec = torch.tensor(oracle.fp8_e4m3_decode_table())[got.long()] * slot_scale[:, None]
+    slot0 = int(bt[0, 0]) * page
+    s0 = slot_scale[slot0]
+    assert torch.allclose(dec[slot0], (v[0, 0] / s0).clamp(-448, 448) * s0, rtol=0.07, atol=s0.item())

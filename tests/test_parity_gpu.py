@@ -424,3 +424,25 @@ def test_auto_path_picks_tile_for_prefill_and_row_for_decode(hyperion):
 
 def test_prefill_config_full_size_sampled_rows(hyperion, oracle):
     _sampled_check(hyperion, oracle, "prefill", n_rows=32, path="tile")
+
+
+def test_forwards_on_two_streams_do_not_share_a_workspace(hyperion, oracle):
+    """Two split-KV decodes enqueued on two streams at once: each stream has its own
+    workspace (work counter, partials), so both results equal the oracle's."""
+    dev = torch.device("cuda", 0)
+    wks = [W.make_dense(f"s{i}", 2, 4, 1, 3000 + 500 * i, o_dtype=torch.float32, seed=60 + i) for i in range(2)]
+    gs = [wk.to(dev) for wk in wks]
+    outs = [g.new_output() for g in gs]
+    streams = [torch.cuda.Stream(dev) for _ in range(2)]
+    torch.cuda.synchronize()
+    for rep in range(3):
+        for g, o, s in zip(gs, outs, streams):
+            with torch.cuda.stream(s):
+                hyperion.hyperion_apex_kernel(g.worklist, g.total_work, g.q, None, g.k, None, g.v, g.v_scale,
+                                              g.ctx_lens, g.block_tables, o, 1, 128, 16, g.block_size, g.num_blocks,
+                                              g.inv_sqrt_d, False, path="row", num_splits=5)
+    torch.cuda.synchronize()
+    for wk, o, s in zip(wks, outs, streams):
+        with torch.cuda.stream(s):
+            assert hyperion.read_device_errors(dev, clear=True) == 0
+        check(oracle, wk, o.cpu().numpy())

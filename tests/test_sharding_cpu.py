@@ -111,3 +111,39 @@ def test_gather_over_two_gloo_ranks(oracle, tmp_path):
         for r in range(world):
             assert np.load(tmp_path / f"r{r}_w{i}_err.npy")[0] == 0
             assert np.array_equal(np.load(tmp_path / f"r{r}_w{i}.npy"), full), (wk.name, r)
+
+
+def _idle_rank_main(rank, world, port, out_dir):
+    """A world larger than the KV heads: the last rank owns no head.  It still takes
+    part in the gather (with an empty block) and computes nothing."""
+    import torch.distributed as dist
+
+    from oracle import oracle as O
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        wk = W.make_paged("gqa_p", 2, 8, [40, 150], page=16, seed=35, o_dtype=torch.float32, kv_heads=2)
+        sub = _shard(wk, world, rank)
+        if sub.total_work:
+            o, _, _, _ = O.forward_workload_c(sub, nthreads=1)
+            o = torch.from_numpy(o)
+        else:
+            o = torch.zeros(0, wk.head_dim)
+        np.save(os.path.join(out_dir, f"idle_r{rank}_n.npy"), np.array([sub.total_work, sub.n_bh]))
+        full = S.gather_output(o, wk.batch, wk.heads, wk.seq_q, kv_group=wk.kv_group)
+        np.save(os.path.join(out_dir, f"idle_r{rank}.npy"), full.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_world_larger_than_kv_heads_leaves_a_rank_idle(oracle, tmp_path):
+    wk = W.make_paged("gqa_p", 2, 8, [40, 150], page=16, seed=35, o_dtype=torch.float32, kv_heads=2)
+    assert len(S.head_range(8, 3, 2, 4)) == 0
+    world = 3
+    mp.spawn(_idle_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    full, _, _, _ = oracle.forward_workload_c(wk)
+    assert np.load(tmp_path / "idle_r2_n.npy").tolist() == [0, 0]
+    for r in range(world):
+        assert np.array_equal(np.load(tmp_path / f"idle_r{r}.npy"), full), r
