@@ -19,16 +19,17 @@ from typing import Dict, Optional, Sequence, Tuple
 import torch
 
 
-def build_worklist(q_lens: torch.Tensor, n_heads: int, kv_signatures: Optional[Sequence[str]] = None,
+def build_worklist(q_lens: torch.Tensor, n_heads: int, kv_signatures: Optional[Sequence] = None,
                    prefetch_hints: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Work items int32 [n, 4] = {q_idx, bh, kv_signature, prefetch_hint} on q_lens' device.
 
     q_lens[b] query rows of sequence b, for each of its n_heads heads; items are
     ordered by (bh = b*n_heads + h, q_idx), the order the forward's tile path reads
-    in 256-item chunks.  kv_signatures (one string per sequence) become 31-bit CRC32
-    values (the reference uses Python's salted hash, which differs between processes);
-    prefetch_hints is an optional int32 [B] bit mask per sequence.  Neither field is
-    read by the forward."""
+    in 256-item chunks.  kv_signatures holds one value per sequence: an int is kept
+    (its low 31 bits: the reference's hash(kv_signature) & 0x7FFFFFFF of a tuple of
+    ints, :923, is the same in every process), a string becomes its 31-bit CRC32
+    (Python's hash of a string is salted per process); prefetch_hints is an optional
+    int32 [B] bit mask per sequence.  Neither field is read by the forward."""
     if q_lens.dim() != 1:
         raise ValueError("q_lens must be 1-D (one length per sequence)")
     dev = q_lens.device
@@ -48,7 +49,8 @@ def build_worklist(q_lens: torch.Tensor, n_heads: int, kv_signatures: Optional[S
     if kv_signatures is not None:
         if len(kv_signatures) != B:
             raise ValueError("one kv_signature per sequence")
-        sig = torch.tensor([zlib.crc32(s.encode()) & 0x7FFFFFFF for s in kv_signatures], dtype=torch.int64, device=dev)
+        sig = torch.tensor([(int(s) if isinstance(s, int) else zlib.crc32(s.encode())) & 0x7FFFFFFF
+                            for s in kv_signatures], dtype=torch.int64, device=dev)
         wl[:, 2] = sig[b_of].to(torch.int32)
     if prefetch_hints is not None:
         wl[:, 3] = prefetch_hints.to(dev, torch.int32)[b_of]
