@@ -26,6 +26,14 @@ namespace {
 thread_local std::string g_last_error;
 thread_local int32_t g_last_call[4] = {0, 0, 0, 0};
 
+// A fault armed by hyperion_debug_fault for the next forward of this thread.
+struct FaultHook {
+  bool armed = false;
+  long long wait_cycles = 0;
+  int stage = -1;
+};
+thread_local FaultHook g_fault;
+
 int fail(int code, const char* msg) {
   g_last_error = msg;
   return code;
@@ -284,6 +292,13 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   p.debug_scores = opt ? opt->debug_scores : nullptr;
   p.debug_ld = opt ? opt->debug_ld : 0;
   if (p.debug_scores && p.debug_ld < 1) return fail(HYPERION_ERR_INVALID_ARG, "debug_ld < 1");
+  p.wait_cycles = hyp::kWaitCycles;
+  p.fault_stage = -1;
+  if (g_fault.armed) {  // consumed by this call
+    p.wait_cycles = g_fault.wait_cycles;
+    p.fault_stage = g_fault.stage;
+    g_fault.armed = false;
+  }
 
   g_last_call[0] = g_last_call[1] = g_last_call[2] = g_last_call[3] = 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -383,6 +398,14 @@ int hyperion_apex_kernel(const int32_t* worklist, int32_t total_work, const uint
   return hyperion_apex_kernel_ex(worklist, total_work, Q, Q_scale, K_cache, K_scale, V_cache, V_scale, context_lens,
                                  block_tables, O, seq_q, head_dim, k_packed_bytes, block_size, num_blocks, inv_sqrt_d,
                                  causal, ext, nullptr, workspace, workspace_bytes, stream);
+}
+
+int hyperion_debug_fault(int64_t wait_cycles, int32_t stage) {
+  if (wait_cycles <= 0) return fail(HYPERION_ERR_INVALID_ARG, "wait_cycles must be > 0");
+  g_fault.armed = true;
+  g_fault.wait_cycles = wait_cycles;
+  g_fault.stage = stage < 0 ? -1 : stage;
+  return HYPERION_OK;
 }
 
 int hyperion_reset_counter(void* workspace, size_t workspace_bytes, void* stream) {

@@ -58,6 +58,8 @@ struct FwdParams {
   long long debug_ld;
   int pages_all_valid;  // 1: every page id the kernels can read is inside the pool (host-checked)
   int o_align32;        // 1: O is 32-byte aligned, so a 16-value row piece is whole 32-byte sectors
+  long long wait_cycles;  // bound of every device wait: kWaitCycles, shorter only under a test hook
+  int fault_stage;        // test hook: index of the KV stage the loading warp leaves unarmed (-1: none)
 };
 
 // KV-side (batch, head) row of query row `bh`: grouped-query attention maps
@@ -105,16 +107,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with parity `parity` to complete.  Returns false (and sets
-// *abort) when the CTA is aborting or the wait exceeded kWaitCycles; the first
-// waiter that times out records HYPERION_DEVERR_WAIT_TIMEOUT.
+// *abort) when the CTA is aborting or the wait exceeded `limit` SM clock cycles
+// (kWaitCycles unless a test shortened it); the first waiter that times out records
+// HYPERION_DEVERR_WAIT_TIMEOUT.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          uint32_t* err) {
+                                          uint32_t* err, long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       raise_error(err, HYPERION_DEVERR_WAIT_TIMEOUT);
       *abort = 1;
       return false;
@@ -126,17 +129,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // 32 lanes (a timeout in one lane fails the wait for the warp), so a warp never
 // splits across a __syncwarp or a .sync.aligned instruction after a timeout.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                               uint32_t* err) {
-  const bool ok = mbar_wait(bar, parity, abort, err);
+                                               uint32_t* err, long long limit) {
+  const bool ok = mbar_wait(bar, parity, abort, err, limit);
   return __all_sync(0xffffffffu, ok);
 }
 
 // Bounded wait that ignores the abort flag: used on the way out of an aborted CTA
 // to let copies already in flight land before the CTA's shared memory is released.
-__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, long long limit) {
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) return;
+    if (clock64() - t0 > limit) return;
   }
 }
 

@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
       t = __shfl_sync(0xffffffffu, t, 0);
       if (t >= total_units) {
         const int us = rc & 1;
-        if (!mbar_wait_warp(&sm.run_empty[us], ((rc >> 1) & 1) ^ 1, abort, p.err)) break;
+        if (!mbar_wait_warp(&sm.run_empty[us], ((rc >> 1) & 1) ^ 1, abort, p.err, p.wait_cycles)) break;
         if (lane == 0) {
           sm.slot[us].unit = -1;
           mbar_arrive(&sm.run_full[us]);
@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
         const int bh_r = __shfl_sync(0xffffffffu, inf.bh, r);
 
         const int us = rc & 1;
-        if (!mbar_wait_warp(&sm.run_empty[us], ((rc >> 1) & 1) ^ 1, abort, p.err)) {
+        if (!mbar_wait_warp(&sm.run_empty[us], ((rc >> 1) & 1) ^ 1, abort, p.err, p.wait_cycles)) {
           aborted = true;
           break;
         }
@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
 
         for (int k0 = k_lo; k0 < k_hi; k0 += kKeysPerStage) {
           const int s = it % kGStages;
-          if (!mbar_wait_warp(&sm.empty[s], ((it / kGStages) & 1) ^ 1, abort, p.err)) {
+          if (!mbar_wait_warp(&sm.empty[s], ((it / kGStages) & 1) ^ 1, abort, p.err, p.wait_cycles)) {
             aborted = true;
             break;
           }
@@ -226,7 +226,10 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
           bytes = __reduce_add_sync(0xffffffffu, bytes);
           mask = ((unsigned long long)__reduce_or_sync(0xffffffffu, (uint32_t)(mask >> 32)) << 32) |
                  __reduce_or_sync(0xffffffffu, (uint32_t)mask);
-          if (lane == 0) {
+          // Test hook: the stage numbered fault_stage is left unarmed, with no copy
+          // in flight on it, so the consumers' wait for it runs out.
+          const bool armed = (int)it != p.fault_stage;
+          if (lane == 0 && armed) {
             sm.hdr[s].nkeys = nk;
             sm.hdr[s].mask = mask;
             if (bytes) {
@@ -236,7 +239,7 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
             }
           }
           __syncwarp();
-          for (int i = lane; i < np; i += 32) {
+          for (int i = lane; armed && i < np; i += 32) {
             const int page = p0 + i;
             const int lo = max(k0, page * bs);
             const int hi = min(k0 + nk, (page + 1) * bs);
@@ -258,7 +261,7 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
     if (*abort && lane == 0) {
       // Let the copies of the last (up to kGStages) armed stages land before exit.
       for (uint32_t i = (it > (uint32_t)kGStages ? it - kGStages : 0u); i < it; ++i)
-        mbar_drain(&sm.full[i % kGStages], (i / kGStages) & 1);
+        mbar_drain(&sm.full[i % kGStages], (i / kGStages) & 1, p.wait_cycles);
     }
   } else {
     // ------------------------------------------------------------ consumers
@@ -267,7 +270,7 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
     uint32_t rc = 0;
     for (;;) {
       const int us = rc & 1;
-      if (!mbar_wait_warp(&sm.run_full[us], (rc >> 1) & 1, abort, p.err)) break;
+      if (!mbar_wait_warp(&sm.run_full[us], (rc >> 1) & 1, abort, p.err, p.wait_cycles)) break;
       ++rc;
       const RunSlot<W>& sl = sm.slot[us];
       if (sl.unit < 0) break;
@@ -286,7 +289,7 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
       bool aborted = false;
       for (int k0 = sl.k_lo; k0 < sl.k_hi; k0 += kKeysPerStage) {
         const int s = it % kGStages;
-        if (!mbar_wait_warp(&sm.full[s], (it / kGStages) & 1, abort, p.err)) {
+        if (!mbar_wait_warp(&sm.full[s], (it / kGStages) & 1, abort, p.err, p.wait_cycles)) {
           aborted = true;
           break;
         }

@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
       t = __shfl_sync(0xffffffffu, t, 0);
       const int unit = (t < total_units) ? t : -1;
       const int us = ucount & 1;
-      if (!mbar_wait_warp(&sm.unit_empty[us], ((ucount >> 1) & 1) ^ 1, abort, p.err)) break;
+      if (!mbar_wait_warp(&sm.unit_empty[us], ((ucount >> 1) & 1) ^ 1, abort, p.err, p.wait_cycles)) break;
       int item = 0, split = 0, k_lo = 0, k_hi = 0, bh = 0, q_idx = 0;
       bool valid = false;
       if (unit >= 0) {
@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
       const int kv = kv_of(p, bh);
       for (int k0 = k_lo; k0 < k_hi; k0 += kKeysPerStage) {
         const int s = it % kStages;
-        if (!mbar_wait_warp(&sm.empty[s], ((it / kStages) & 1) ^ 1, abort, p.err)) {
+        if (!mbar_wait_warp(&sm.empty[s], ((it / kStages) & 1) ^ 1, abort, p.err, p.wait_cycles)) {
           aborted = true;
           break;
         }
@@ -210,7 +210,10 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
         bytes = __reduce_add_sync(0xffffffffu, bytes);
         mask = ((unsigned long long)__reduce_or_sync(0xffffffffu, (uint32_t)(mask >> 32)) << 32) |
                __reduce_or_sync(0xffffffffu, (uint32_t)mask);
-        if (lane == 0) {
+        // Test hook: the stage numbered fault_stage is left unarmed, with no copy in
+        // flight on it, so the consumers' wait for it runs out.
+        const bool armed = (int)it != p.fault_stage;
+        if (lane == 0 && armed) {
           sm.hdr[s].nkeys = n;
           sm.hdr[s].mask = mask;
           if (bytes) {
@@ -220,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
           }
         }
         __syncwarp();
-        for (int i = lane; i < np; i += 32) {
+        for (int i = lane; armed && i < np; i += 32) {
           const int page = p0 + i;
           const int lo = max(k0, page * bs);
           const int hi = min(k0 + n, (page + 1) * bs);
@@ -239,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
     if (*abort && lane == 0) {
       // Let the copies of the last (up to kStages) armed stages land before exit.
       for (uint32_t i = (it > (uint32_t)kStages ? it - kStages : 0u); i < it; ++i)
-        mbar_drain(&sm.full[i % kStages], (i / kStages) & 1);
+        mbar_drain(&sm.full[i % kStages], (i / kStages) & 1, p.wait_cycles);
     }
   } else {
     // ------------------------------------------------------------ consumers
@@ -248,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
     uint32_t ucount = 0;
     for (;;) {
       const int us = ucount & 1;
-      if (!mbar_wait_warp(&sm.unit_full[us], (ucount >> 1) & 1, abort, p.err)) break;
+      if (!mbar_wait_warp(&sm.unit_full[us], (ucount >> 1) & 1, abort, p.err, p.wait_cycles)) break;
       const UnitSlot sl = sm.slot[us];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.unit_empty[us]);
@@ -272,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
       bool aborted = false;
       for (int k0 = sl.k_lo; k0 < sl.k_hi; k0 += kKeysPerStage) {
         const int s = it % kStages;
-        if (!mbar_wait_warp(&sm.full[s], (it / kStages) & 1, abort, p.err)) {
+        if (!mbar_wait_warp(&sm.full[s], (it / kStages) & 1, abort, p.err, p.wait_cycles)) {
           aborted = true;
           break;
         }

@@ -425,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       // Take the next ticket only once every role has started the previous unit:
       // the metadata of unit uc is then ready one unit ahead, and no CTA holds a
       // ticket it will not start soon (the tail stays balanced).
-      if (uc >= 1 && !mbar_wait_warp(&sm.sched_empty[(uc - 1) & 1], ((uc - 1) >> 1) & 1, abort, p.err)) break;
+      if (uc >= 1 && !mbar_wait_warp(&sm.sched_empty[(uc - 1) & 1], ((uc - 1) >> 1) & 1, abort, p.err, p.wait_cycles)) break;
       int c = -1;
       for (;;) {
         int t = 0;
@@ -441,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         }
       }
       if (c < 0) {
-        if (!mbar_wait_warp(&sm.sched_empty[uc & 1], ((uc >> 1) & 1) ^ 1, abort, p.err)) break;
+        if (!mbar_wait_warp(&sm.sched_empty[uc & 1], ((uc >> 1) & 1) ^ 1, abort, p.err, p.wait_cycles)) break;
         if (lane == 0) {
           sm.unit[uc & 1].kind = 0;
           mbar_arrive(&sm.sched_full[uc & 1]);
@@ -492,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         }
         const int kv_len = p.causal ? min(ctx, maxq + 1) : ctx;
         const int n_tiles = (kv_len + kKeys - 1) / kKeys;
-        if (!mbar_wait_warp(&sm.sched_empty[uc & 1], ((uc >> 1) & 1) ^ 1, abort, p.err)) {
+        if (!mbar_wait_warp(&sm.sched_empty[uc & 1], ((uc >> 1) & 1) ^ 1, abort, p.err, p.wait_cycles)) {
           stop = true;
           break;
         }
@@ -528,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     uint32_t uc = 0, rit = 0;
     bool stop = false;
     while (!stop) {
-      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) break;
+      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err, p.wait_cycles)) break;
       const UnitInfo u = sm.unit[uc & 1];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.sched_empty[uc & 1]);
@@ -540,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         const int n_tiles = u.n_tiles;
         for (int j = 0; j < n_tiles; ++j) {
           const int r = rit % kRawStages;
-          if (!mbar_wait_warp(&sm.raw_empty[r], ((rit / kRawStages) & 1) ^ 1, abort, p.err)) {
+          if (!mbar_wait_warp(&sm.raw_empty[r], ((rit / kRawStages) & 1) ^ 1, abort, p.err, p.wait_cycles)) {
             stop = true;
             break;
           }
@@ -570,7 +570,10 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           bytes = __reduce_add_sync(0xffffffffu, bytes);
 #pragma unroll
           for (int w = 0; w < 4; ++w) mk[w] = __reduce_or_sync(0xffffffffu, mk[w]);
-          if (lane == 0) {
+          // Test hook: the raw stage numbered fault_stage is left unarmed, with no
+          // copy in flight on it, so the converters' wait for it runs out.
+          const bool armed = (int)rit != p.fault_stage;
+          if (lane == 0 && armed) {
 #pragma unroll
             for (int w = 0; w < 4; ++w) sm.raw_mask[r][w] = mk[w];
             if (bytes) {
@@ -580,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
             }
           }
           __syncwarp();
-          for (int i = lane; i < np; i += 32) {
+          for (int i = lane; armed && i < np; i += 32) {
             const int page = p0 + i;
             const int lo = max(k0, page * bs);
             const int hi = min(k0 + n, (page + 1) * bs);
@@ -598,7 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     }
     if (*abort && lane == 0) {
       for (uint32_t i = (rit > (uint32_t)kRawStages ? rit - kRawStages : 0u); i < rit; ++i)
-        mbar_drain(&sm.raw_full[i % kRawStages], (i / kRawStages) & 1);
+        mbar_drain(&sm.raw_full[i % kRawStages], (i / kRawStages) & 1, p.wait_cycles);
     }
   } else if (warp >= kConvWarp0 && warp < kConvWarp0 + kConvWarps) {
     // ================================================================ converters
@@ -606,7 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     uint32_t uc = 0, rit = 0, kvit = 0, uq = 0;
     const uint32_t q_base = smem_u32(&sm.q[0][0]);
     for (;;) {
-      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) break;
+      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err, p.wait_cycles)) break;
       const UnitInfo u = sm.unit[uc & 1];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.sched_empty[uc & 1]);
@@ -615,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       if (u.n_tiles == 0) continue;
       // ---- Q rows of the unit -> e4m3 +-1, K-major SW128 (a negative inv_sqrt_d is
       // folded in by flipping every bit: the scores change sign)
-      if (!mbar_wait_warp(&sm.q_empty, (uq & 1) ^ 1, abort, p.err)) break;
+      if (!mbar_wait_warp(&sm.q_empty, (uq & 1) ^ 1, abort, p.err, p.wait_cycles)) break;
 #pragma unroll
       for (int i = 0; i < kQTiles; ++i) {
         const int r = i * kRows + ct;
@@ -641,8 +644,8 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       for (int j = 0; j < u.n_tiles; ++j) {
         const int r = rit % kRawStages;
         const int s = kvit % kKvStages;
-        if (!mbar_wait_warp(&sm.raw_full[r], (rit / kRawStages) & 1, abort, p.err) ||
-            !mbar_wait_warp(&sm.kv_empty[s], ((kvit / kKvStages) & 1) ^ 1, abort, p.err)) {
+        if (!mbar_wait_warp(&sm.raw_full[r], (rit / kRawStages) & 1, abort, p.err, p.wait_cycles) ||
+            !mbar_wait_warp(&sm.kv_empty[s], ((kvit / kKvStages) & 1) ^ 1, abort, p.err, p.wait_cycles)) {
           ab = true;
           break;
         }
@@ -725,17 +728,17 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           tc::mma_f16_ts(o_tm, s_tm + 64u * h + 8u * kk, bd + 128 * kk, tc::kIdescPV, (acc || kk > 0) ? 1u : 0u);
       };
       for (;;) {
-        if (!mbar_wait(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) break;
+        if (!mbar_wait(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err, p.wait_cycles)) break;
         const UnitInfo u = sm.unit[uc & 1];
         mbar_arrive(&sm.sched_empty[uc & 1]);
         ++uc;
         if (u.kind == 0) break;
         const int n = u.n_tiles;
         if (n == 0) continue;
-        if (!mbar_wait(&sm.q_full, uq & 1, abort, p.err)) break;
+        if (!mbar_wait(&sm.q_full, uq & 1, abort, p.err, p.wait_cycles)) break;
         ++uq;
         int s = kvit % kKvStages;
-        if (!mbar_wait(&sm.kv_full[s], (kvit / kKvStages) & 1, abort, p.err)) break;
+        if (!mbar_wait(&sm.kv_full[s], (kvit / kKvStages) & 1, abort, p.err, p.wait_cycles)) break;
         tc::fence_after_sync();
         qk(s, 0);
         tc::commit(&sm.s_full[t][0]);
@@ -748,15 +751,15 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           const uint32_t nxt = g + 1;
           const int s2 = nxt % kKvStages;
           // ---- half A
-          if (!mbar_wait(&sm.p_full[t][0], g & 1, abort, p.err) ||
-              (j == 0 && !mbar_wait(&sm.o_empty[t], (uo & 1) ^ 1, abort, p.err))) {
+          if (!mbar_wait(&sm.p_full[t][0], g & 1, abort, p.err, p.wait_cycles) ||
+              (j == 0 && !mbar_wait(&sm.o_empty[t], (uo & 1) ^ 1, abort, p.err, p.wait_cycles))) {
             ab = true;
             break;
           }
           tc::fence_after_sync();
           pv(s, 0, j > 0);
           if (j + 1 < n) {
-            if (!mbar_wait(&sm.kv_full[s2], (nxt / kKvStages) & 1, abort, p.err)) {
+            if (!mbar_wait(&sm.kv_full[s2], (nxt / kKvStages) & 1, abort, p.err, p.wait_cycles)) {
               ab = true;
               break;
             }
@@ -765,7 +768,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
             tc::commit(&sm.s_full[t][0]);
           }
           // ---- half B
-          if (!mbar_wait(&sm.p_full[t][1], g & 1, abort, p.err)) {
+          if (!mbar_wait(&sm.p_full[t][1], g & 1, abort, p.err, p.wait_cycles)) {
             ab = true;
             break;
           }
@@ -785,7 +788,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       }
       // Every MMA issued must land before TMEM is released.
       tc::commit(&sm.drain[t]);
-      mbar_drain(&sm.drain[t], 0);
+      mbar_drain(&sm.drain[t], 0, p.wait_cycles);
     }
     __syncwarp();
   } else {
@@ -810,7 +813,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     UnitInfo nu;
     int n_qi = -1;
     auto fetch = [&]() -> bool {
-      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) return false;
+      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err, p.wait_cycles)) return false;
       nu = sm.unit[uc & 1];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.sched_empty[uc & 1]);
@@ -841,7 +844,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       for (int j = 0; j < n_tiles; ++j) {
         const uint32_t g = kvit;
         const int s = g % kKvStages;
-        if (!mbar_wait_warp(&sm.s_full[t][0], g & 1, abort, p.err)) {
+        if (!mbar_wait_warp(&sm.s_full[t][0], g & 1, abort, p.err, p.wait_cycles)) {
           ab = true;
           break;
         }
@@ -849,7 +852,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         if (!p.pages_all_valid) {
           // Page ids can fall outside the pool: read the tile's key mask (the
           // converters copied it before completing this phase of kv_full).
-          if (!mbar_wait_warp(&sm.kv_full[s], (g / kKvStages) & 1, abort, p.err)) {
+          if (!mbar_wait_warp(&sm.kv_full[s], (g / kKvStages) & 1, abort, p.err, p.wait_cycles)) {
             ab = true;
             break;
           }
@@ -868,7 +871,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           // Both halves' scores are needed first.  S of half B ready also means the
           // PV of tile g-1 is done (it was issued before that QK), so O may be
           // rescaled here.
-          if (!mbar_wait_warp(&sm.s_full[t][1], g & 1, abort, p.err)) {
+          if (!mbar_wait_warp(&sm.s_full[t][1], g & 1, abort, p.err, p.wait_cycles)) {
             ab = true;
             break;
           }
@@ -904,7 +907,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         if (lane == 0) mbar_arrive(&sm.p_full[t][0]);
         // ---- half B: keys 64-127, P over S columns 64-95
         if (!have_b) {
-          if (!mbar_wait_warp(&sm.s_full[t][1], g & 1, abort, p.err)) {
+          if (!mbar_wait_warp(&sm.s_full[t][1], g & 1, abort, p.err, p.wait_cycles)) {
             ab = true;
             break;
           }
@@ -921,7 +924,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       if (ab) break;
       have = fetch();
       // ---- epilogue: O row = acc * 256 * vscale / l
-      if (!mbar_wait_warp(&sm.o_full[t], oc & 1, abort, p.err)) break;
+      if (!mbar_wait_warp(&sm.o_full[t], oc & 1, abort, p.err, p.wait_cycles)) break;
       ++oc;
       tc::fence_after_sync();
       const float vs = u.vs;

@@ -285,6 +285,17 @@ def read_device_errors(device=None, clear: bool = True) -> int:
     return int(flags.value)
 
 
+def debug_fault(wait_cycles: int, stage: int = -1) -> None:
+    """Test hook of the bounded device waits (hyperion_debug_fault): the next forward
+    on this thread bounds every device wait by `wait_cycles` SM clocks and, for
+    stage >= 0, leaves that KV stage of its key stream unarmed so the first wait on
+    it runs out.  That forward then raises DEVERR_WAIT_TIMEOUT (read_device_errors)
+    and leaves its output incomplete; the device stays usable."""
+    rc = _capi.lib.hyperion_debug_fault(int(wait_cycles), int(stage))
+    if rc != _capi.HYPERION_OK:
+        raise RuntimeError(f"hyperion_debug_fault failed (status {rc}): {_capi.last_error()}")
+
+
 def launch_info() -> dict:
     """Launch facts derived from the current device (SM count, CTAs per SM, shared memory)."""
     keys = ("sm_count", "row_ctas_per_sm", "row_smem_bytes", "tile_ctas_per_sm", "tile_smem_bytes",

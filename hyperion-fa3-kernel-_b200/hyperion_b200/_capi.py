@@ -46,6 +46,7 @@ EXPORTED = (
     "hyperion_version",
     "hyperion_apex_kernel_noalloc",
     "hyperion_kv_cache_write",
+    "hyperion_debug_fault",
 )
 
 # Fixed per-device scratch of hyperion_apex_kernel_noalloc (HYPERION_NOALLOC_SCRATCH_BYTES).
@@ -121,6 +122,8 @@ def _load() -> ctypes.CDLL:
     lib.hyperion_kv_cache_write.restype = ctypes.c_int
     lib.hyperion_kv_cache_write.argtypes = [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _i64, _i32, _i32, _vp, _i64,
                                             _vp, _vp, _i64, _vp, ctypes.c_size_t, _vp]
+    lib.hyperion_debug_fault.restype = ctypes.c_int
+    lib.hyperion_debug_fault.argtypes = [_i64, _i32]
     return lib
 
 

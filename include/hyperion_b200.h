@@ -148,6 +148,20 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work,
  * on its own stream, and this call zeroes it explicitly (asynchronous on `stream`). */
 int hyperion_reset_counter(void* workspace, size_t workspace_bytes, void* stream);
 
+/* Test hook for the bounded device waits; it has no counterpart in the reference,
+ * whose kernel waits without a bound.  Arms a fault for the next forward issued on
+ * this host thread (hyperion_apex_kernel, _ex or _noalloc), then disarms:
+ *   - every device wait of that call gives up after `wait_cycles` SM clock cycles
+ *     instead of about one second;
+ *   - when `stage` >= 0, the warp that streams the keys leaves the stage-th KV stage
+ *     it would load unarmed, with no copy in flight on it, so the first wait on it
+ *     runs out.
+ * The call still returns HYPERION_OK; on the device the wait that runs out raises
+ * HYPERION_DEVERR_WAIT_TIMEOUT, the kernel unwinds (copies and MMAs in flight land,
+ * tensor memory is freed) and returns with its output incomplete, and the device
+ * and the workspace stay usable for the next call.  wait_cycles must be > 0. */
+int hyperion_debug_fault(int64_t wait_cycles, int32_t stage);
+
 /* Synchronises `stream`, returns the accumulated HYPERION_DEVERR_* flags of this
  * workspace in *flags and clears them when `clear` is non-zero. */
 int hyperion_read_device_errors(void* workspace, size_t workspace_bytes, void* stream,
