@@ -60,6 +60,9 @@ SPEC_PEAKS = {"hbm_gbs": 7700.0, "bf16_tflops": 2250.0}
 METRIC = "attn Q·KV-token pairs/s"
 L2_BYTES = 126 << 20
 SUB_WORKLOADS = ("decode", "paged_decode", "decode_gqa", "longctx")
+GATHER_CHUNKS = 4   # runs of (batch, head) rows whose O gathers overlap the next run's compute
+GATHER_SMS = 16     # SMs the forward leaves to NCCL while a gather runs beside it
+NVLINK_GBS = 770.0  # measured peer-copy bandwidth per direction per GPU on this machine type
 
 
 def peaks():
@@ -563,38 +566,72 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
     e2e_ms, h2d, d2h, e2e_mode = run_e2e(hyperion, wk, o, args, barrier)
 
     # N > 1: the same steps with the all-gather of O (NCCL) inside each step, for a
-    # caller that wants the whole output on every rank.
-    gather_total = 0.0
+    # caller that wants the whole output on every rank.  Two forms: the forward then
+    # one gather (serial), and the forward in GATHER_CHUNKS runs of (batch, head) rows
+    # whose gathers (on a second stream) overlap the next run's compute, with the
+    # forward's persistent grid kept off GATHER_SMS SMs so that NCCL's kernels find
+    # room beside it.
+    gather_total = serial_total = 0.0
     if world > 1:
+        from hyperion_b200 import sharding as S
+
         out_all = torch.empty((world,) + tuple(o.shape), dtype=o.dtype, device=dev)
-        pg.all_gather_into_tensor(out_all, o)
-        torch.cuda.synchronize()
-        g_st = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        g_en = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        barrier()
-        torch.cuda.synchronize()
-        for i in range(args.steps):
-            if flush is not None:
-                flush.fill_(i & 0xFF)
-            g_st[i].record(stream)
+        chunks = S.row_chunks(wk, GATHER_CHUNKS)
+        rows_c = chunks[0][1].stop - chunks[0][1].start
+        out_chunks = torch.empty((len(chunks), world, rows_c) + tuple(o.shape[1:]), dtype=o.dtype, device=dev)
+        comm = torch.cuda.Stream(dev)
+        budget = max(1, torch.cuda.get_device_properties(dev).multi_processor_count - GATHER_SMS)
+
+        def forward_chunk(items):
+            wl = wk.worklist[items]
+            hyperion.hyperion_apex_kernel(wl, wl.shape[0], wk.q, None, wk.k, None, wk.v, wk.v_scale, wk.ctx_lens,
+                                          wk.block_tables, o, wk.seq_q, wk.head_dim, wk.head_dim // 8, wk.block_size,
+                                          wk.num_blocks, wk.inv_sqrt_d, wk.causal, path=args.path,
+                                          kv_group=wk.kv_group, sm_budget=budget)
+
+        def serial_step():
             call_forward(hyperion, wk, o, path=args.path)
             pg.all_gather_into_tensor(out_all, o)
-            g_en[i].record(stream)
-        torch.cuda.synchronize()
-        barrier()
-        gather_total = sum(s.elapsed_time(e) for s, e in zip(g_st, g_en))
-        del out_all
 
-    vals = torch.tensor([total_ms, e2e_ms, float(pairs), gather_total], dtype=torch.float64, device=dev)
+        def overlapped_step():
+            S.forward_and_gather(forward_chunk, chunks, o, out_chunks, comm_stream=comm)
+
+        totals = []
+        for step in (serial_step, overlapped_step):
+            step()
+            torch.cuda.synchronize()
+            g_st = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+            g_en = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+            barrier()
+            torch.cuda.synchronize()
+            for i in range(args.steps):
+                if flush is not None:
+                    flush.fill_(i & 0xFF)
+                g_st[i].record(stream)
+                step()
+                g_en[i].record(stream)
+            torch.cuda.synchronize()
+            barrier()
+            totals.append(sum(s.elapsed_time(e) for s, e in zip(g_st, g_en)))
+        serial_total, gather_total = totals
+        # The overlapped output is the serial one, rank by rank (a chunked call may
+        # choose other KV splits, so the two agree to rounding, not bit for bit).
+        diff = (out_chunks.transpose(0, 1).reshape(out_all.shape).float() - out_all.float()).abs().max().item()
+        if not diff <= 2e-2:
+            raise RuntimeError(f"overlapped gather differs from the serial gather by {diff}")
+        del out_all, out_chunks
+
+    vals = torch.tensor([total_ms, e2e_ms, float(pairs), gather_total, serial_total], dtype=torch.float64,
+                        device=dev)
     if pg is not None:
         mx = vals.clone()
         pg.all_reduce(mx, op=pg.ReduceOp.MAX)
         sm = vals.clone()
         pg.all_reduce(sm, op=pg.ReduceOp.SUM)
-        total_ms_max, e2e_ms_max, gather_max = float(mx[0]), float(mx[1]), float(mx[3])
+        total_ms_max, e2e_ms_max, gather_max, serial_max = float(mx[0]), float(mx[1]), float(mx[3]), float(mx[4])
         pairs_all = float(sm[2])
     else:
-        total_ms_max, e2e_ms_max, gather_max = total_ms, e2e_ms, 0.0
+        total_ms_max, e2e_ms_max, gather_max, serial_max = total_ms, e2e_ms, 0.0, 0.0
         pairs_all = float(pairs)
 
     rec = None
@@ -635,11 +672,18 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
         if roof["bound"] == "hbm":
             rec["hbm_gbs"] = roof["achieved"]
         if world > 1:
+            o_bytes = o.numel() * o.element_size()
             rec["with_gather"] = {
                 "value": pairs_all * args.steps / (gather_max * 1e-3), "unit": "pairs/s",
                 "ms_per_step": gather_max / args.steps,
-                "gather_bytes_per_rank": o.numel() * o.element_size() * world,
-                "mode": "forward + NCCL all_gather_into_tensor of O in every step, max over ranks",
+                "serial_ms_per_step": serial_max / args.steps,
+                "gather_bytes_received_per_rank": o_bytes * (world - 1),
+                "nvlink_floor_ms": o_bytes * (world - 1) / NVLINK_GBS / 1e6,
+                "mode": (f"forward in {GATHER_CHUNKS} runs of (batch, head) rows on {GATHER_SMS} fewer SMs, each run's "
+                         "O all-gathered (NCCL all_gather_into_tensor, second stream) while the next computes; "
+                         "serial_ms_per_step: the forward, then one all-gather; max over ranks"),
+                "limiter": ("NVLink: each rank receives (world-1) x its O bytes; the floor is that over the measured "
+                            f"{NVLINK_GBS:.0f} GB/s peer-copy bandwidth per direction"),
             }
     del wk, o, flush
     torch.cuda.empty_cache()

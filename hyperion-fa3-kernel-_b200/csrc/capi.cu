@@ -20,6 +20,7 @@
 #include "row_group_kernel.cuh"
 #include "tile_kernel.cuh"
 #include "kv_write.cuh"
+#include "launch_table.h"
 
 namespace {
 
@@ -115,12 +116,37 @@ int get_dev(const DevInfo** out) {
   return HYPERION_OK;
 }
 
-// KV splits per item of the row kernel.  A worklist that alone gives every CTA
-// slot about 16 units is not split.  A shorter one is split until it does, and
-// at least into pieces of at most 8192 keys of the table; no piece is shorter
-// than 512 keys, and an item has at most 16 pieces.
+// The measured split count for a call of `kernel` (0 row kernel, 1 grouped row
+// kernel with 4 query heads per KV head) with `items` work items of up to `keys`
+// keys, or 0 when the launch table (launch_table.h, written by tune_launch.py from a
+// sweep on B200) has no entry within a factor of 2 of both, or was measured on
+// another SM count or head_dim.
+int table_splits(const DevInfo& di, int kernel, int D, long long items, long long keys) {
+  if (D != 128 || di.n_sm != hyp::table::kSplitTableSms || items <= 0 || keys <= 0) return 0;
+  int best = 0;
+  double best_d = 1e30;
+  for (const hyp::table::SplitEntry& e : hyp::table::kSplitTable) {
+    if (e.kernel != kernel) continue;
+    const double di_ = std::fabs(std::log2((double)items / e.items));
+    const double dk = std::fabs(std::log2((double)keys / e.keys));
+    if (di_ > 1.0 || dk > 1.0) continue;
+    if (di_ + dk < best_d) {
+      best_d = di_ + dk;
+      best = e.splits;
+    }
+  }
+  return best;
+}
+
+// KV splits per item of the row kernel: the launch table's measured count near the
+// call's shape, else this rule.  A worklist that alone gives every CTA slot about
+// 16 units is not split.  A shorter one is split until it does, and at least into
+// pieces of at most 8192 keys of the table; no piece is shorter than 512 keys, and
+// an item has at most 16 pieces.
 int choose_splits(const DevInfo& di, int D, int total_work, long long max_keys) {
   if (total_work <= 0) return 1;
+  const int measured = table_splits(di, 0, D, total_work, max_keys);
+  if (measured > 0) return measured;
   const int ctas = (D == 256) ? di.row_ctas_256 : di.row_ctas_128;
   const long long target = (long long)di.n_sm * ctas * 16;
   if (total_work >= target) return 1;
@@ -131,15 +157,23 @@ int choose_splits(const DevInfo& di, int D, int total_work, long long max_keys) 
   return (int)std::max<long long>(ns, 1);
 }
 
-// KV splits per unit of the grouped row kernel, whose unit holds up to 4 work
-// items: enough units for 4 per CTA slot and, while units are scarce (fewer than
-// 16 per slot), pieces of at most 2048 keys so that ragged contexts balance; no
-// piece shorter than 512 keys, at most 16 pieces.  (Paged decode with 32 query
-// heads over 8 KV heads, contexts U[512, 32768]: 1.21 ms at 13-16 pieces against
-// 1.27 ms at the row kernel's choice of 4 in isolated calls; the same 1.26 ms under
-// the sustained power cap, where the whole step with host copies gains 4 %.)
-int choose_group_splits(const DevInfo& di, int D, long long chunks, long long max_keys) {
-  if (chunks <= 0) return 1;
+// KV splits per unit of the grouped row kernel, whose unit holds up to
+// group_items (at most 4) work items.  Decode with 4 query heads per KV head takes
+// the launch table's measured count near its shape; otherwise the rule: enough
+// units for 4 per CTA slot and, while units are scarce (fewer than 16 per slot),
+// pieces of at most 2048 keys so that ragged contexts balance; no piece shorter
+// than 512 keys, at most 16 pieces.  (Paged decode with 32 query heads over 8 KV
+// heads, contexts U[512, 32768]: 1.21 ms at 13-16 pieces against 1.27 ms at the row
+// kernel's choice of 4 in isolated calls; the same 1.26 ms under the sustained
+// power cap, where the whole step with host copies gains 4 %.)
+int choose_group_splits(const DevInfo& di, int D, long long items, int group_items, bool decode,
+                        long long max_keys) {
+  if (items <= 0) return 1;
+  if (decode && group_items == 4) {
+    const int measured = table_splits(di, 1, D, items, max_keys);
+    if (measured > 0) return measured;
+  }
+  const long long chunks = (items + group_items - 1) / group_items;
   const long long slots = (long long)di.n_sm * ((D == 256) ? di.group_ctas_256 : di.group_ctas_128);
   if (chunks >= 16 * slots) return 1;
   long long ns = (4 * slots + chunks - 1) / chunks;
@@ -159,8 +193,9 @@ size_t partial_bytes(int total_work, int n_split, int D) {
 // The grouped kernel's choice is bounded by its smallest unit count, 4 items a unit.
 size_t workspace_needed(const DevInfo& di, int total_work, int D, int block_size, int num_blocks) {
   const long long max_keys = (long long)std::max(block_size, 1) * std::max(num_blocks, 1);
-  const int ns = std::max(choose_splits(di, D, total_work, max_keys),
-                          choose_group_splits(di, D, ((long long)total_work + 3) / 4, max_keys));
+  const int ns = std::max({choose_splits(di, D, total_work, max_keys),
+                           choose_group_splits(di, D, total_work, 4, true, max_keys),
+                           choose_group_splits(di, D, total_work, 4, false, max_keys)});
   return hyp::kWsPartials + partial_bytes(total_work, ns, D);
 }
 
@@ -168,7 +203,7 @@ size_t workspace_needed(const DevInfo& di, int total_work, int D, int block_size
 
 extern "C" {
 
-int32_t hyperion_version(void) { return 1 * 10000 + 0 * 100 + 0; }
+int32_t hyperion_version(void) { return 1 * 10000 + 1 * 100 + 0; }
 
 const char* hyperion_last_error_string(void) { return g_last_error.c_str(); }
 
@@ -227,6 +262,7 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   if (ext->o_dtype != HYPERION_DTYPE_F16 && ext->o_dtype != HYPERION_DTYPE_BF16 && ext->o_dtype != HYPERION_DTYPE_F32)
     return fail(HYPERION_ERR_INVALID_ARG, "o_dtype is not F16, BF16 or F32");
   if (opt && opt->kv_group < 0) return fail(HYPERION_ERR_INVALID_ARG, "kv_group < 0");
+  if (opt && opt->sm_budget < 0) return fail(HYPERION_ERR_INVALID_ARG, "sm_budget < 0");
   const int kv_group = (opt && opt->kv_group > 1) ? opt->kv_group : 1;
   if ((long long)ext->n_bh * kv_group > 0x7fffffffLL)
     return fail(HYPERION_ERR_INVALID_ARG, "n_bh * kv_group exceeds int32");
@@ -253,6 +289,8 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   if (rc) return rc;
 
   const int path_req = opt ? opt->path : HYPERION_PATH_AUTO;
+  // SMs the persistent grids are sized for: all of them, or the caller's budget.
+  const int sm_use = (opt && opt->sm_budget > 0) ? std::min<int>(opt->sm_budget, di->n_sm) : di->n_sm;
   if (path_req != HYPERION_PATH_AUTO && path_req != HYPERION_PATH_ROW && path_req != HYPERION_PATH_TILE)
     return fail(HYPERION_ERR_INVALID_ARG, "unknown path");
 
@@ -321,7 +359,7 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
     e = cudaMemsetAsync(ws + hyp::kWsCounters, 0, 64, st);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(counters)");
     int grid = 0;
-    rc = hyp::tile::launch(p, di->n_sm, di->tile_ctas, di->tile_smem, st, &grid);
+    rc = hyp::tile::launch(p, sm_use, di->tile_ctas, di->tile_smem, st, &grid);
     if (rc) return rc;
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "tile kernel launch");
@@ -340,7 +378,8 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   p.group_items = !grouped ? 1 : (kv_group > 1) ? std::min(kv_group, hyp::row::kGroupMax) : hyp::row::kGroupMax;
   const long long chunks = ((long long)total_work + p.group_items - 1) / p.group_items;
   int ns = (opt && opt->num_splits > 0) ? std::min(opt->num_splits, 16)
-           : grouped                    ? choose_group_splits(*di, head_dim, chunks, max_keys)
+           : grouped                    ? choose_group_splits(*di, head_dim, total_work, p.group_items, seq_q == 1,
+                                                                  max_keys)
                                         : choose_splits(*di, head_dim, total_work, max_keys);
   const size_t need = hyp::kWsPartials + partial_bytes(total_work, ns, head_dim);
   if (workspace_bytes < need) return fail(HYPERION_ERR_WORKSPACE, "workspace smaller than hyperion_workspace_bytes()");
@@ -355,7 +394,7 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
     const long long gunits = chunks * ns;
     const int ctas = (head_dim == 256) ? di->group_ctas_256 : di->group_ctas_128;
     const int smem = (head_dim == 256) ? di->group_smem_256 : di->group_smem_128;
-    grid = (int)std::min<long long>(gunits, (long long)di->n_sm * ctas);
+    grid = (int)std::min<long long>(gunits, (long long)sm_use * ctas);
     if (head_dim == 256) {
       hyp::row::row_group_kernel<256><<<grid, hyp::row::kGThreads, smem, st>>>(p, (int)gunits);
     } else {
@@ -364,7 +403,7 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   } else {
     const int ctas = (head_dim == 256) ? di->row_ctas_256 : di->row_ctas_128;
     const int smem = (head_dim == 256) ? di->row_smem_256 : di->row_smem_128;
-    grid = (int)std::min<long long>(units, (long long)di->n_sm * ctas);
+    grid = (int)std::min<long long>(units, (long long)sm_use * ctas);
     if (head_dim == 256) {
       hyp::row::row_fwd_kernel<256><<<grid, hyp::row::kThreads, smem, st>>>(p, (int)units);
     } else {
@@ -548,7 +587,7 @@ extern "C" int hyperion_apex_kernel_noalloc(const int32_t* worklist, int32_t tot
     const long long max_keys = (long long)block_size * num_blocks;
     // The split count the forward chose: a query row per (batch, head) takes the
     // row kernel, several take the grouped kernel (4 work items a unit).
-    const int ns = (seq_q > 1) ? choose_group_splits(*di, head_dim, ((long long)total_work + 3) / 4, max_keys)
+    const int ns = (seq_q > 1) ? choose_group_splits(*di, head_dim, total_work, 4, false, max_keys)
                                : choose_splits(*di, head_dim, total_work, max_keys);
     char msg[320];
     std::snprintf(msg, sizeof(msg),

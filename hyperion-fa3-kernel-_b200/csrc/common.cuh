@@ -106,31 +106,44 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase with parity `parity` to complete.  Returns false (and sets
-// *abort) when the CTA is aborting or the wait exceeded `limit` SM clock cycles
-// (kWaitCycles unless a test shortened it); the first waiter that times out records
-// HYPERION_DEVERR_WAIT_TIMEOUT.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          uint32_t* err, long long limit) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Abort flag and wait bound of a CTA, kept in its shared memory: the flag is set
+// by the first wait that runs out, and every other wait then gives up.
+struct WaitCtl {
+  int flag;
+  int pad;
+  long long limit;  // SM clock cycles a wait may take: kWaitCycles unless a test shortened it
+};
+
+// The spinning part of mbar_wait, kept out of line: the kernels have a few dozen
+// wait sites, and one shared copy of the loop keeps their code small.
+__device__ __noinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile WaitCtl* ctl, uint32_t* err) {
   const long long t0 = clock64();
+  const long long limit = ctl->limit;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort) return false;
+    if (ctl->flag) return false;
     if (clock64() - t0 > limit) {
       raise_error(err, HYPERION_DEVERR_WAIT_TIMEOUT);
-      *abort = 1;
+      ctl->flag = 1;
       return false;
     }
   }
 }
 
+// Waits for the phase with parity `parity` to complete.  Returns false (and sets
+// the CTA's abort flag) when the CTA is aborting or the wait exceeded ctl->limit SM
+// clock cycles; the first waiter that times out records HYPERION_DEVERR_WAIT_TIMEOUT.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile WaitCtl* ctl, uint32_t* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_spin(bar, parity, ctl, err);
+}
+
 // mbar_wait for a whole warp: every lane waits, and the outcome is the same in all
 // 32 lanes (a timeout in one lane fails the wait for the warp), so a warp never
 // splits across a __syncwarp or a .sync.aligned instruction after a timeout.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                               uint32_t* err, long long limit) {
-  const bool ok = mbar_wait(bar, parity, abort, err, limit);
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile WaitCtl* ctl,
+                                               uint32_t* err) {
+  const bool ok = mbar_wait(bar, parity, ctl, err);
   return __all_sync(0xffffffffu, ok);
 }
 

@@ -69,7 +69,7 @@ struct GroupSmem {
   alignas(8) uint64_t empty[NS];
   alignas(8) uint64_t run_full[2];
   alignas(8) uint64_t run_empty[2];
-  int abort;
+  WaitCtl ctl;  // abort flag and wait bound of the CTA
 };
 
 // Resident CTAs per SM the register budget is set for.  The kernel is bound by
@@ -109,12 +109,13 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
       mbar_init(&sm.run_full[s], 1);
       mbar_init(&sm.run_empty[s], kGWarps);
     }
-    sm.abort = 0;
+    sm.ctl.flag = 0;
+    sm.ctl.limit = p.wait_cycles;
     fence_mbar_init();
   }
   __syncthreads();
 
-  volatile int* abort = &sm.abort;
+  volatile WaitCtl* abort = &sm.ctl;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -128,7 +129,7 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
       t = __shfl_sync(0xffffffffu, t, 0);
       if (t >= total_units) {
         const int us = rc & 1;
-        if (!mbar_wait_warp(&sm.run_empty[us], ((rc >> 1) & 1) ^ 1, abort, p.err, p.wait_cycles)) break;
+        if (!mbar_wait_warp(&sm.run_empty[us], ((rc >> 1) & 1) ^ 1, abort, p.err)) break;
         if (lane == 0) {
           sm.slot[us].unit = -1;
           mbar_arrive(&sm.run_full[us]);
@@ -170,7 +171,7 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
         const int bh_r = __shfl_sync(0xffffffffu, inf.bh, r);
 
         const int us = rc & 1;
-        if (!mbar_wait_warp(&sm.run_empty[us], ((rc >> 1) & 1) ^ 1, abort, p.err, p.wait_cycles)) {
+        if (!mbar_wait_warp(&sm.run_empty[us], ((rc >> 1) & 1) ^ 1, abort, p.err)) {
           aborted = true;
           break;
         }
@@ -199,7 +200,7 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
 
         for (int k0 = k_lo; k0 < k_hi; k0 += kKeysPerStage) {
           const int s = it % kGStages;
-          if (!mbar_wait_warp(&sm.empty[s], ((it / kGStages) & 1) ^ 1, abort, p.err, p.wait_cycles)) {
+          if (!mbar_wait_warp(&sm.empty[s], ((it / kGStages) & 1) ^ 1, abort, p.err)) {
             aborted = true;
             break;
           }
@@ -258,7 +259,7 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
       }
       if (aborted) break;
     }
-    if (*abort && lane == 0) {
+    if (abort->flag && lane == 0) {
       // Let the copies of the last (up to kGStages) armed stages land before exit.
       for (uint32_t i = (it > (uint32_t)kGStages ? it - kGStages : 0u); i < it; ++i)
         mbar_drain(&sm.full[i % kGStages], (i / kGStages) & 1, p.wait_cycles);
@@ -270,7 +271,7 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
     uint32_t rc = 0;
     for (;;) {
       const int us = rc & 1;
-      if (!mbar_wait_warp(&sm.run_full[us], (rc >> 1) & 1, abort, p.err, p.wait_cycles)) break;
+      if (!mbar_wait_warp(&sm.run_full[us], (rc >> 1) & 1, abort, p.err)) break;
       ++rc;
       const RunSlot<W>& sl = sm.slot[us];
       if (sl.unit < 0) break;
@@ -289,7 +290,7 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
       bool aborted = false;
       for (int k0 = sl.k_lo; k0 < sl.k_hi; k0 += kKeysPerStage) {
         const int s = it % kGStages;
-        if (!mbar_wait_warp(&sm.full[s], (it / kGStages) & 1, abort, p.err, p.wait_cycles)) {
+        if (!mbar_wait_warp(&sm.full[s], (it / kGStages) & 1, abort, p.err)) {
           aborted = true;
           break;
         }
@@ -484,7 +485,7 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
       }
       // Every consumer warp reaches the named barriers below for every query of the
       // run, also when it gave up on a wait: the barriers have no timeout of their own.
-      const bool stop = aborted || (*abort != 0);
+      const bool stop = aborted || (abort->flag != 0);
       const float vs_run = (p.v_scale_mode == 2) ? 1.f : v_scale_for(p, sl.bh0, 0);
 
       // ---- merge the consumer warps' (m, l, acc), two queries per round ----

@@ -76,7 +76,7 @@ struct Smem {
   alignas(8) uint64_t empty[kStages];
   alignas(8) uint64_t unit_full[2];
   alignas(8) uint64_t unit_empty[2];
-  int abort;
+  WaitCtl ctl;  // abort flag and wait bound of the CTA
 };
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -129,12 +129,13 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
       mbar_init(&sm.unit_full[s], 1);
       mbar_init(&sm.unit_empty[s], kConsumerWarps);
     }
-    sm.abort = 0;
+    sm.ctl.flag = 0;
+    sm.ctl.limit = p.wait_cycles;
     fence_mbar_init();
   }
   __syncthreads();
 
-  volatile int* abort = &sm.abort;
+  volatile WaitCtl* abort = &sm.ctl;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -147,7 +148,7 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
       t = __shfl_sync(0xffffffffu, t, 0);
       const int unit = (t < total_units) ? t : -1;
       const int us = ucount & 1;
-      if (!mbar_wait_warp(&sm.unit_empty[us], ((ucount >> 1) & 1) ^ 1, abort, p.err, p.wait_cycles)) break;
+      if (!mbar_wait_warp(&sm.unit_empty[us], ((ucount >> 1) & 1) ^ 1, abort, p.err)) break;
       int item = 0, split = 0, k_lo = 0, k_hi = 0, bh = 0, q_idx = 0;
       bool valid = false;
       if (unit >= 0) {
@@ -183,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
       const int kv = kv_of(p, bh);
       for (int k0 = k_lo; k0 < k_hi; k0 += kKeysPerStage) {
         const int s = it % kStages;
-        if (!mbar_wait_warp(&sm.empty[s], ((it / kStages) & 1) ^ 1, abort, p.err, p.wait_cycles)) {
+        if (!mbar_wait_warp(&sm.empty[s], ((it / kStages) & 1) ^ 1, abort, p.err)) {
           aborted = true;
           break;
         }
@@ -239,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
       }
       if (aborted) break;
     }
-    if (*abort && lane == 0) {
+    if (abort->flag && lane == 0) {
       // Let the copies of the last (up to kStages) armed stages land before exit.
       for (uint32_t i = (it > (uint32_t)kStages ? it - kStages : 0u); i < it; ++i)
         mbar_drain(&sm.full[i % kStages], (i / kStages) & 1, p.wait_cycles);
@@ -251,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
     uint32_t ucount = 0;
     for (;;) {
       const int us = ucount & 1;
-      if (!mbar_wait_warp(&sm.unit_full[us], (ucount >> 1) & 1, abort, p.err, p.wait_cycles)) break;
+      if (!mbar_wait_warp(&sm.unit_full[us], (ucount >> 1) & 1, abort, p.err)) break;
       const UnitSlot sl = sm.slot[us];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.unit_empty[us]);
@@ -275,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
       bool aborted = false;
       for (int k0 = sl.k_lo; k0 < sl.k_hi; k0 += kKeysPerStage) {
         const int s = it % kStages;
-        if (!mbar_wait_warp(&sm.full[s], (it / kStages) & 1, abort, p.err, p.wait_cycles)) {
+        if (!mbar_wait_warp(&sm.full[s], (it / kStages) & 1, abort, p.err)) {
           aborted = true;
           break;
         }
@@ -392,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
       }
       // Every consumer warp reaches both named barriers below once per unit, also
       // when it gave up on a wait: the barriers have no timeout of their own.
-      const bool stop = aborted || (*abort != 0);
+      const bool stop = aborted || (abort->flag != 0);
 
       // ---- merge the consumer warps' (m, l, acc) ----
       const float l_warp = warp_sum(l);

@@ -102,7 +102,7 @@ struct Smem {
   alignas(8) uint64_t o_empty[kQTiles];
   alignas(8) uint64_t drain[kQTiles];
   uint32_t tmem_base;
-  int abort;
+  WaitCtl ctl;  // abort flag and wait bound of the CTA
 };
 
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + alignment slack of the dynamic base
@@ -395,7 +395,8 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       mbar_init(&sm.o_empty[t], 4);
       mbar_init(&sm.drain[t], 1);
     }
-    sm.abort = 0;
+    sm.ctl.flag = 0;
+    sm.ctl.limit = p.wait_cycles;
     fence_mbar_init();
   }
   if (warp == kMmaWarp) {
@@ -406,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = sm.tmem_base;
-  volatile int* abort = &sm.abort;
+  volatile WaitCtl* abort = &sm.ctl;
 
   if (warp == kSchedWarp) {
     // ================================================================ scheduler
@@ -425,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       // Take the next ticket only once every role has started the previous unit:
       // the metadata of unit uc is then ready one unit ahead, and no CTA holds a
       // ticket it will not start soon (the tail stays balanced).
-      if (uc >= 1 && !mbar_wait_warp(&sm.sched_empty[(uc - 1) & 1], ((uc - 1) >> 1) & 1, abort, p.err, p.wait_cycles)) break;
+      if (uc >= 1 && !mbar_wait_warp(&sm.sched_empty[(uc - 1) & 1], ((uc - 1) >> 1) & 1, abort, p.err)) break;
       int c = -1;
       for (;;) {
         int t = 0;
@@ -441,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         }
       }
       if (c < 0) {
-        if (!mbar_wait_warp(&sm.sched_empty[uc & 1], ((uc >> 1) & 1) ^ 1, abort, p.err, p.wait_cycles)) break;
+        if (!mbar_wait_warp(&sm.sched_empty[uc & 1], ((uc >> 1) & 1) ^ 1, abort, p.err)) break;
         if (lane == 0) {
           sm.unit[uc & 1].kind = 0;
           mbar_arrive(&sm.sched_full[uc & 1]);
@@ -492,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         }
         const int kv_len = p.causal ? min(ctx, maxq + 1) : ctx;
         const int n_tiles = (kv_len + kKeys - 1) / kKeys;
-        if (!mbar_wait_warp(&sm.sched_empty[uc & 1], ((uc >> 1) & 1) ^ 1, abort, p.err, p.wait_cycles)) {
+        if (!mbar_wait_warp(&sm.sched_empty[uc & 1], ((uc >> 1) & 1) ^ 1, abort, p.err)) {
           stop = true;
           break;
         }
@@ -528,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     uint32_t uc = 0, rit = 0;
     bool stop = false;
     while (!stop) {
-      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err, p.wait_cycles)) break;
+      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) break;
       const UnitInfo u = sm.unit[uc & 1];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.sched_empty[uc & 1]);
@@ -540,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         const int n_tiles = u.n_tiles;
         for (int j = 0; j < n_tiles; ++j) {
           const int r = rit % kRawStages;
-          if (!mbar_wait_warp(&sm.raw_empty[r], ((rit / kRawStages) & 1) ^ 1, abort, p.err, p.wait_cycles)) {
+          if (!mbar_wait_warp(&sm.raw_empty[r], ((rit / kRawStages) & 1) ^ 1, abort, p.err)) {
             stop = true;
             break;
           }
@@ -599,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         }
       }
     }
-    if (*abort && lane == 0) {
+    if (abort->flag && lane == 0) {
       for (uint32_t i = (rit > (uint32_t)kRawStages ? rit - kRawStages : 0u); i < rit; ++i)
         mbar_drain(&sm.raw_full[i % kRawStages], (i / kRawStages) & 1, p.wait_cycles);
     }
@@ -609,7 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     uint32_t uc = 0, rit = 0, kvit = 0, uq = 0;
     const uint32_t q_base = smem_u32(&sm.q[0][0]);
     for (;;) {
-      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err, p.wait_cycles)) break;
+      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) break;
       const UnitInfo u = sm.unit[uc & 1];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.sched_empty[uc & 1]);
@@ -618,7 +619,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       if (u.n_tiles == 0) continue;
       // ---- Q rows of the unit -> e4m3 +-1, K-major SW128 (a negative inv_sqrt_d is
       // folded in by flipping every bit: the scores change sign)
-      if (!mbar_wait_warp(&sm.q_empty, (uq & 1) ^ 1, abort, p.err, p.wait_cycles)) break;
+      if (!mbar_wait_warp(&sm.q_empty, (uq & 1) ^ 1, abort, p.err)) break;
 #pragma unroll
       for (int i = 0; i < kQTiles; ++i) {
         const int r = i * kRows + ct;
@@ -644,8 +645,8 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       for (int j = 0; j < u.n_tiles; ++j) {
         const int r = rit % kRawStages;
         const int s = kvit % kKvStages;
-        if (!mbar_wait_warp(&sm.raw_full[r], (rit / kRawStages) & 1, abort, p.err, p.wait_cycles) ||
-            !mbar_wait_warp(&sm.kv_empty[s], ((kvit / kKvStages) & 1) ^ 1, abort, p.err, p.wait_cycles)) {
+        if (!mbar_wait_warp(&sm.raw_full[r], (rit / kRawStages) & 1, abort, p.err) ||
+            !mbar_wait_warp(&sm.kv_empty[s], ((kvit / kKvStages) & 1) ^ 1, abort, p.err)) {
           ab = true;
           break;
         }
@@ -728,17 +729,17 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           tc::mma_f16_ts(o_tm, s_tm + 64u * h + 8u * kk, bd + 128 * kk, tc::kIdescPV, (acc || kk > 0) ? 1u : 0u);
       };
       for (;;) {
-        if (!mbar_wait(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err, p.wait_cycles)) break;
+        if (!mbar_wait(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) break;
         const UnitInfo u = sm.unit[uc & 1];
         mbar_arrive(&sm.sched_empty[uc & 1]);
         ++uc;
         if (u.kind == 0) break;
         const int n = u.n_tiles;
         if (n == 0) continue;
-        if (!mbar_wait(&sm.q_full, uq & 1, abort, p.err, p.wait_cycles)) break;
+        if (!mbar_wait(&sm.q_full, uq & 1, abort, p.err)) break;
         ++uq;
         int s = kvit % kKvStages;
-        if (!mbar_wait(&sm.kv_full[s], (kvit / kKvStages) & 1, abort, p.err, p.wait_cycles)) break;
+        if (!mbar_wait(&sm.kv_full[s], (kvit / kKvStages) & 1, abort, p.err)) break;
         tc::fence_after_sync();
         qk(s, 0);
         tc::commit(&sm.s_full[t][0]);
@@ -751,15 +752,15 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           const uint32_t nxt = g + 1;
           const int s2 = nxt % kKvStages;
           // ---- half A
-          if (!mbar_wait(&sm.p_full[t][0], g & 1, abort, p.err, p.wait_cycles) ||
-              (j == 0 && !mbar_wait(&sm.o_empty[t], (uo & 1) ^ 1, abort, p.err, p.wait_cycles))) {
+          if (!mbar_wait(&sm.p_full[t][0], g & 1, abort, p.err) ||
+              (j == 0 && !mbar_wait(&sm.o_empty[t], (uo & 1) ^ 1, abort, p.err))) {
             ab = true;
             break;
           }
           tc::fence_after_sync();
           pv(s, 0, j > 0);
           if (j + 1 < n) {
-            if (!mbar_wait(&sm.kv_full[s2], (nxt / kKvStages) & 1, abort, p.err, p.wait_cycles)) {
+            if (!mbar_wait(&sm.kv_full[s2], (nxt / kKvStages) & 1, abort, p.err)) {
               ab = true;
               break;
             }
@@ -768,7 +769,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
             tc::commit(&sm.s_full[t][0]);
           }
           // ---- half B
-          if (!mbar_wait(&sm.p_full[t][1], g & 1, abort, p.err, p.wait_cycles)) {
+          if (!mbar_wait(&sm.p_full[t][1], g & 1, abort, p.err)) {
             ab = true;
             break;
           }
@@ -813,7 +814,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     UnitInfo nu;
     int n_qi = -1;
     auto fetch = [&]() -> bool {
-      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err, p.wait_cycles)) return false;
+      if (!mbar_wait_warp(&sm.sched_full[uc & 1], (uc >> 1) & 1, abort, p.err)) return false;
       nu = sm.unit[uc & 1];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.sched_empty[uc & 1]);
@@ -844,7 +845,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       for (int j = 0; j < n_tiles; ++j) {
         const uint32_t g = kvit;
         const int s = g % kKvStages;
-        if (!mbar_wait_warp(&sm.s_full[t][0], g & 1, abort, p.err, p.wait_cycles)) {
+        if (!mbar_wait_warp(&sm.s_full[t][0], g & 1, abort, p.err)) {
           ab = true;
           break;
         }
@@ -852,7 +853,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         if (!p.pages_all_valid) {
           // Page ids can fall outside the pool: read the tile's key mask (the
           // converters copied it before completing this phase of kv_full).
-          if (!mbar_wait_warp(&sm.kv_full[s], (g / kKvStages) & 1, abort, p.err, p.wait_cycles)) {
+          if (!mbar_wait_warp(&sm.kv_full[s], (g / kKvStages) & 1, abort, p.err)) {
             ab = true;
             break;
           }
@@ -871,7 +872,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           // Both halves' scores are needed first.  S of half B ready also means the
           // PV of tile g-1 is done (it was issued before that QK), so O may be
           // rescaled here.
-          if (!mbar_wait_warp(&sm.s_full[t][1], g & 1, abort, p.err, p.wait_cycles)) {
+          if (!mbar_wait_warp(&sm.s_full[t][1], g & 1, abort, p.err)) {
             ab = true;
             break;
           }
@@ -907,7 +908,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         if (lane == 0) mbar_arrive(&sm.p_full[t][0]);
         // ---- half B: keys 64-127, P over S columns 64-95
         if (!have_b) {
-          if (!mbar_wait_warp(&sm.s_full[t][1], g & 1, abort, p.err, p.wait_cycles)) {
+          if (!mbar_wait_warp(&sm.s_full[t][1], g & 1, abort, p.err)) {
             ab = true;
             break;
           }
@@ -924,7 +925,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       if (ab) break;
       have = fetch();
       // ---- epilogue: O row = acc * 256 * vscale / l
-      if (!mbar_wait_warp(&sm.o_full[t], oc & 1, abort, p.err, p.wait_cycles)) break;
+      if (!mbar_wait_warp(&sm.o_full[t], oc & 1, abort, p.err)) break;
       ++oc;
       tc::fence_after_sync();
       const float vs = u.vs;

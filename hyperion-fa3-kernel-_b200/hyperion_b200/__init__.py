@@ -52,7 +52,7 @@ from ._capi import (  # noqa: F401
 )
 
 HYPERION_LOADED = True
-__version__ = "1.0.0"
+__version__ = "1.1.0"
 
 _O_DTYPES = {torch.float16: _capi.DTYPE_F16, torch.bfloat16: _capi.DTYPE_BF16, torch.float32: _capi.DTYPE_F32}
 _PATHS = {"auto": _capi.PATH_AUTO, "row": _capi.PATH_ROW, "tile": _capi.PATH_TILE}
@@ -124,6 +124,7 @@ def hyperion_apex_kernel(
     num_splits: int = 0,
     debug_scores: Optional[torch.Tensor] = None,
     kv_group: int = 1,
+    sm_budget: int = 0,
 ) -> None:
     """Enqueues the forward on the current CUDA stream of O's device (asynchronous).
 
@@ -137,6 +138,9 @@ def hyperion_apex_kernel(
     context_lens, the block-table rows, the contiguous layout and a per-head
     V_scale by the KV row bh // kv_group.  The row path streams each KV stage once
     for up to 4 consecutive work items on the same KV row.
+
+    `sm_budget` (0: all): SMs the persistent kernels may occupy, for a caller that
+    overlaps a collective on another stream with the forward.
     """
     total_work = int(total_work)
     _check(int(kv_group) >= 1, "kv_group must be >= 1")
@@ -190,7 +194,7 @@ def hyperion_apex_kernel(
                         _hint(grid), _hint(block), _hint(shared))
     opt = _capi.Options(_PATHS[path], int(num_splits),
                         debug_scores.data_ptr() if debug_scores is not None else None,
-                        debug_scores.size(1) if debug_scores is not None else 0, int(kv_group))
+                        debug_scores.size(1) if debug_scores is not None else 0, int(kv_group), int(sm_budget))
     with torch.cuda.device(dev):
         need = _capi.lib.hyperion_workspace_bytes(total_work, head_dim, block_size, num_blocks)
         _check(need > 0, f"hyperion_workspace_bytes failed: {_capi.last_error()}")

@@ -73,6 +73,7 @@ class Options(ctypes.Structure):
         ("debug_scores", ctypes.c_void_p),
         ("debug_ld", ctypes.c_int64),
         ("kv_group", ctypes.c_int32),
+        ("sm_budget", ctypes.c_int32),
     ]
 
 

@@ -100,6 +100,52 @@ def assemble_heads(parts: List[torch.Tensor], batch: int, n_heads: int, seq_q: i
     return out.reshape(batch * n_heads * seq_q, d)
 
 
+def row_chunks(wk: Workload, n_chunks: int) -> List[tuple]:
+    """(work items, O rows) of n_chunks equal runs of (batch, head) rows of a workload
+    whose worklist is the dense one in (bh, q_idx) order: each run's items and O rows
+    are then each one contiguous range."""
+    per = wk.seq_q
+    if wk.total_work != wk.n_bh * per:
+        raise ValueError("row_chunks needs the dense (bh, q_idx) worklist")
+    if n_chunks < 1 or wk.n_bh % n_chunks:
+        raise ValueError(f"{wk.n_bh} (batch, head) rows do not split into {n_chunks} equal chunks")
+    step = wk.n_bh // n_chunks * per
+    return [(slice(c * step, (c + 1) * step), slice(c * step, (c + 1) * step)) for c in range(n_chunks)]
+
+
+def forward_and_gather(forward_chunk, chunks, o_local: torch.Tensor, out: torch.Tensor, group=None,
+                       comm_stream=None) -> None:
+    """Runs the forward chunk by chunk and all-gathers each chunk's O while the next
+    chunk computes.
+
+    forward_chunk(items) enqueues the forward of the work items `items` (a slice of the
+    worklist) on the current stream; chunks is a list of equal (items, O rows) slices
+    in row order, such as row_chunks gives.  out: [n_chunks, world, rows of a chunk,
+    D]: out[c, r] receives rank r's O rows of chunk c, so rank r's whole output is
+    out[:, r] in chunk order (out.transpose(0, 1), without a copy).  The
+    gathers run on comm_stream (a new stream when None) once their chunk is computed;
+    the current stream waits for the last one before this returns.  Every rank of
+    `group` must call this with the same chunk sizes, in the same order of
+    collectives."""
+    import torch.distributed as dist
+
+    if not o_local.is_cuda:  # host tensors (a CPU process group): one chunk after the other
+        for c, (items, rows) in enumerate(chunks):
+            forward_chunk(items)
+            dist.all_gather_into_tensor(out[c].view(-1, *o_local.shape[1:]), o_local[rows], group=group)
+        return
+    cur = torch.cuda.current_stream(o_local.device)
+    comm = comm_stream or torch.cuda.Stream(o_local.device)
+    for c, (items, rows) in enumerate(chunks):
+        forward_chunk(items)
+        done = torch.cuda.Event()
+        done.record(cur)
+        comm.wait_event(done)
+        with torch.cuda.stream(comm):
+            dist.all_gather_into_tensor(out[c].view(-1, *o_local.shape[1:]), o_local[rows], group=group)
+    cur.wait_stream(comm)
+
+
 def gather_output(o_local: torch.Tensor, batch: int, n_heads: int, seq_q: int, group=None,
                   kv_group: int = 1) -> torch.Tensor:
     """All-gathers the head-block outputs of every rank into the full O on each rank.

@@ -107,6 +107,11 @@ typedef struct hyperion_options {
                             items on the same KV row.  No counterpart in the reference,
                             whose engine config has num_kv_heads (hyperion_fa3_production_final.py:853)
                             but whose kernel reads one KV row per (batch, head). */
+  int32_t sm_budget;     /* SMs the forward's persistent kernels may occupy; 0 = all of them.
+                            A caller that runs a collective (an NCCL all-gather of O, say)
+                            on another stream during the forward leaves the rest to it: the
+                            kernels size their grids to sm_budget SMs.  No counterpart in
+                            the reference.  Added in version 1.1.0. */
 } hyperion_options;
 
 /* Bytes of device workspace the forward needs for these sizes with the automatic

@@ -31,7 +31,7 @@ def test_library_loads_and_exports_every_declared_symbol(hyperion):
     lib = ctypes.CDLL(hyperion.library_path())
     for name in _declared_functions():
         assert hasattr(lib, name), name
-    assert lib.hyperion_version() == 10000
+    assert lib.hyperion_version() == 10100
 
 
 def test_drop_in_names_match_reference_module(hyperion):
@@ -147,3 +147,25 @@ def test_c_boundary_accepts_an_empty_call_from_an_idle_rank(hyperion):
     rc = _capi.lib.hyperion_apex_kernel(None, 0, None, None, None, None, None, None, None, None, None, 1, 96, 12,
                                         16, 1, ctypes.c_float(0.088), 1, ctypes.byref(ext), None, 0, None)
     assert rc == _capi.HYPERION_ERR_UNSUPPORTED
+
+
+def test_launch_table_is_a_measured_grid():
+    """csrc/launch_table.h (written by tune_launch.py from a sweep on B200) holds one
+    entry per measured shape: split counts among the swept candidates, and for each
+    entry the time of its split no worse than the rule's at the same shape."""
+    import os
+    import re
+
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "hyperion-fa3-kernel-_b200",
+                        "csrc", "launch_table.h")
+    text = open(path).read()
+    assert "kSplitTableSms = 148" in text
+    rows = re.findall(r"\{(\d), (\d+), (\d+), (\d+)\},\s+// ([\d.]+) ms; the rule's (\d+): ([\d.]+) ms", text)
+    assert len(rows) >= 30
+    seen = set()
+    for kernel, items, keys, splits, best_ms, rule, rule_ms in rows:
+        assert (kernel, items, keys) not in seen
+        seen.add((kernel, items, keys))
+        assert int(splits) in (1, 2, 3, 4, 6, 8, 12, 16)
+        assert float(best_ms) <= float(rule_ms) * 1.01
+    assert {k for k, _, _ in seen} == {"0", "1"}

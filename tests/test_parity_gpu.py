@@ -446,3 +446,48 @@ def test_forwards_on_two_streams_do_not_share_a_workspace(hyperion, oracle):
         with torch.cuda.stream(s):
             assert hyperion.read_device_errors(dev, clear=True) == 0
         check(oracle, wk, o.cpu().numpy())
+
+
+@pytest.mark.parametrize("kv_heads,splits", [(None, 8), (8, 16)])
+def test_split_choice_follows_the_measured_table(hyperion, oracle, kv_heads, splits):
+    """On a 148-SM B200 the automatic split count for a shape the launch table
+    measured is the table's (128 query rows x 8192 keys: 8 pieces on the row kernel;
+    the same with 4 query heads per KV head: 16 pieces on the grouped kernel), and the
+    result is still the oracle's."""
+    if hyperion.launch_info()["sm_count"] != 148:
+        pytest.skip("the launch table was measured on 148 SMs")
+    wk = W.make_dense("t", 4, 32, 1, 8192, kv_heads=kv_heads, o_dtype=torch.float32, seed=66)
+    dev = torch.device("cuda", 0)
+    g = wk.to(dev)
+    o = g.new_output()
+    hyperion.hyperion_apex_kernel(g.worklist, g.total_work, g.q, None, g.k, None, g.v, g.v_scale, g.ctx_lens,
+                                  g.block_tables, o, 1, 128, 16, g.block_size, g.num_blocks, g.inv_sqrt_d, False,
+                                  kv_group=g.kv_group)
+    info = hyperion.last_call_info()
+    assert info["splits"] == splits, info
+    rows = list(range(0, g.n_bh, 7))
+    check(oracle, wk, o.cpu().numpy(), rows=rows)
+
+
+@pytest.mark.parametrize("path,seq_q", [("tile", 256), ("row", 1)])
+def test_sm_budget_caps_the_persistent_grid(hyperion, oracle, path, seq_q):
+    """sm_budget keeps the persistent kernels on that many SMs (the rest stay free for
+    a collective on another stream); the result does not change."""
+    wk = W.make_dense("b", 4, 16, seq_q, 1024 if seq_q == 1 else seq_q, causal=seq_q > 1, o_dtype=torch.float32,
+                      seed=67)
+    dev = torch.device("cuda", 0)
+    g = wk.to(dev)
+    info = hyperion.launch_info()
+    o = g.new_output()
+    hyperion.hyperion_apex_kernel(g.worklist, g.total_work, g.q, None, g.k, None, g.v, g.v_scale, g.ctx_lens,
+                                  g.block_tables, o, g.seq_q, 128, 16, g.block_size, g.num_blocks, g.inv_sqrt_d,
+                                  g.causal, path=path, sm_budget=10)
+    grid = hyperion.last_call_info()["grid"]
+    per_sm = info["tile_ctas_per_sm"] if path == "tile" else info["row_ctas_per_sm"]
+    assert grid <= 10 * per_sm, grid
+    assert hyperion.read_device_errors(dev, clear=True) == 0
+    check(oracle, wk, o.cpu().numpy())
+    with pytest.raises(RuntimeError, match="sm_budget"):
+        hyperion.hyperion_apex_kernel(g.worklist, g.total_work, g.q, None, g.k, None, g.v, g.v_scale, g.ctx_lens,
+                                      g.block_tables, o, g.seq_q, 128, 16, g.block_size, g.num_blocks, g.inv_sqrt_d,
+                                      g.causal, path=path, sm_budget=-1)

@@ -147,3 +147,52 @@ def test_world_larger_than_kv_heads_leaves_a_rank_idle(oracle, tmp_path):
     assert np.load(tmp_path / "idle_r2_n.npy").tolist() == [0, 0]
     for r in range(world):
         assert np.array_equal(np.load(tmp_path / f"idle_r{r}.npy"), full), r
+
+
+def _chunked_rank_main(rank, world, port, out_dir):
+    """Each rank computes its head block one batch entry at a time and all-gathers
+    each entry's O as it is done (forward_and_gather); the oracle stands in for the
+    kernel."""
+    import torch.distributed as dist
+
+    from oracle import oracle as O
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        wk = W.make_dense("c", 3, 4, 20, 20, causal=True, o_dtype=torch.float32, seed=37)
+        sub = _shard(wk, world, rank)
+        o_local = torch.zeros(sub.n_bh * sub.seq_q, sub.head_dim)
+        done = []
+
+        def forward_chunk(items):
+            piece = W.Workload(**{**sub.__dict__, "worklist": sub.worklist[items]})
+            o, written, _, _ = O.forward_workload_c(piece, nthreads=1)
+            rows = (piece.worklist[:, 1].long() * sub.seq_q + piece.worklist[:, 0].long())
+            o_local[rows] = torch.from_numpy(o)[rows]
+            done.append(items)
+
+        chunks = S.row_chunks(sub, 3)
+        rows_c = chunks[0][1].stop - chunks[0][1].start
+        out = torch.empty(len(chunks), world, rows_c, sub.head_dim)
+        S.forward_and_gather(forward_chunk, chunks, o_local, out)
+        parts = list(out.transpose(0, 1).reshape(world, -1, sub.head_dim))
+        full = S.assemble_heads(parts, wk.batch, wk.heads, wk.seq_q, world)
+        np.save(os.path.join(out_dir, f"chunked_r{rank}.npy"), full.numpy())
+        np.save(os.path.join(out_dir, f"chunked_r{rank}_n.npy"), np.array([len(done)]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_chunked_forward_and_gather_over_two_gloo_ranks(oracle, tmp_path):
+    """The overlapped gather's bookkeeping: chunks of (batch, head) rows, out[c, r] holding
+    rank r's chunk c, and out.transpose(0, 1) giving each rank's head block in order,
+    which assemble into the single-process result."""
+    world = 2
+    mp.spawn(_chunked_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    wk = W.make_dense("c", 3, 4, 20, 20, causal=True, o_dtype=torch.float32, seed=37)
+    full, _, _, _ = oracle.forward_workload_c(wk)
+    for r in range(world):
+        assert np.load(tmp_path / f"chunked_r{r}_n.npy")[0] == 3
+        assert np.array_equal(np.load(tmp_path / f"chunked_r{r}.npy"), full), r
