@@ -16,7 +16,8 @@ data-path collective).  The same line carries sub-records, measured in the same
 run with the same method, for the decode workloads (whose metric is HBM GB/s)
 and the long-context prefill (B1 H64 S32768, heads split over the ranks:
 strong scaling).  At N > 1 every record also carries `with_gather`: the same
-steps with the all-gather of O (NCCL) inside each step.
+steps with the all-gather of O (NCCL) inside each step, serial and overlapped
+with the forward (the faster one is its value).
 
 Timing: W untimed warm-up steps; L2 flushed (256 MiB write) before every timed
 step unless the inputs are larger than twice the L2; each step bracketed by CUDA
@@ -673,15 +674,19 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
             rec["hbm_gbs"] = roof["achieved"]
         if world > 1:
             o_bytes = o.numel() * o.element_size()
+            best = min(gather_max, serial_max)
             rec["with_gather"] = {
-                "value": pairs_all * args.steps / (gather_max * 1e-3), "unit": "pairs/s",
-                "ms_per_step": gather_max / args.steps,
+                "value": pairs_all * args.steps / (best * 1e-3), "unit": "pairs/s",
+                "ms_per_step": best / args.steps,
+                "form": "overlapped" if gather_max <= serial_max else "serial",
+                "overlapped_ms_per_step": gather_max / args.steps,
                 "serial_ms_per_step": serial_max / args.steps,
                 "gather_bytes_received_per_rank": o_bytes * (world - 1),
                 "nvlink_floor_ms": o_bytes * (world - 1) / NVLINK_GBS / 1e6,
-                "mode": (f"forward in {GATHER_CHUNKS} runs of (batch, head) rows on {GATHER_SMS} fewer SMs, each run's "
-                         "O all-gathered (NCCL all_gather_into_tensor, second stream) while the next computes; "
-                         "serial_ms_per_step: the forward, then one all-gather; max over ranks"),
+                "mode": (f"the faster of two forms, max over ranks: overlapped = the forward in {GATHER_CHUNKS} runs of "
+                         f"(batch, head) rows on {GATHER_SMS} fewer SMs, each run's O all-gathered (NCCL "
+                         "all_gather_into_tensor, second stream) while the next computes; serial = the forward, then "
+                         "one all-gather"),
                 "limiter": ("NVLink: each rank receives (world-1) x its O bytes; the floor is that over the measured "
                             f"{NVLINK_GBS:.0f} GB/s peer-copy bandwidth per direction"),
             }

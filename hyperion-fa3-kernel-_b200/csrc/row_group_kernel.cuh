@@ -35,6 +35,10 @@ constexpr int kGThreads = 32 * (1 + kGWarps);
 // KV ring depth: 2 stages, so that 10 CTAs (head_dim 128) or 5 (head_dim 256) fit
 // an SM's shared memory.
 constexpr int kGroupStages = 2;
+// A query's running max is moved only when a 32-key group's max exceeds it by more
+// than ln 4: the weights exp(s - m) then stay at most 4, so a group's f16 sums of
+// w * v stay below 32 * 4 * 448 = 57344, inside the f16 range.
+constexpr float kGroupTau = 1.3862943611198906f;
 
 template <int W>
 struct RunSlot {
@@ -64,7 +68,7 @@ struct GroupSmem {
   float merge_m[kGWarps][2];  // two queries of the run per merge round
   float merge_l[kGWarps][2];
   float merge_acc[kGWarps][2][D];
-  alignas(16) uint32_t wbuf[kGWarps][kGroupMax][kGKeysPerWarp];  // f16x2 {w, w} per query and key
+  alignas(16) uint32_t wbuf[kGWarps][kGKeysPerWarp][kGroupMax];  // f16x2 {w, w} per key and query
   alignas(8) uint64_t full[NS];
   alignas(8) uint64_t empty[NS];
   alignas(8) uint64_t run_full[2];
@@ -353,15 +357,21 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
               any = ext != INT_MAX;
             }
             if (any) {
+              // The running max moves only when the group's max exceeds it by more
+              // than kGroupTau (every first group does: m = -inf); otherwise the
+              // weights exp(s - m) stay below 4 and the rescale is skipped.  The
+              // normalised result is the same: m cancels between acc and l.
               const float mt = (float)ext * p.inv_sqrt_d;
               const float sc = (float)si * p.inv_sqrt_d;
-              const float m_new = fmaxf(m[j], mt);
-              const float alpha = (m[j] == -INFINITY) ? 0.f : exp_clamped(m[j] - m_new);
-              w[j] = ok ? exp_clamped(sc - m_new) : 0.f;
-              l[j] = l[j] * alpha + w[j];
+              if (mt > m[j] + kGroupTau) {
+                const float alpha = (m[j] == -INFINITY) ? 0.f : exp_clamped(m[j] - mt);
+                l[j] *= alpha;
 #pragma unroll
-              for (int i = 0; i < DPL; ++i) acc[j][i] *= alpha;
-              m[j] = m_new;
+                for (int i = 0; i < DPL; ++i) acc[j][i] *= alpha;
+                m[j] = mt;
+              }
+              w[j] = ok ? exp_clamped(sc - m[j]) : 0.f;
+              l[j] += w[j];
               any_all = true;
             }
           }
@@ -376,9 +386,11 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
           if (!exact) {
             // f16x2 products of the hardware decode, shared by the run's queries;
             // see row_fwd_kernel for the ranges and the NaN rule.
+            // A lane's weights of every query go to one 16-byte row of wbuf, so the
+            // product loop reads all of a key's weights with one broadcast load.
             if (lane < kGKeysPerWarp) {
 #pragma unroll
-              for (int j = 0; j < JN; ++j) sm.wbuf[cw][j][lane] = pack_f16x2(w[j], w[j]);
+              for (int j = 0; j < JN; ++j) sm.wbuf[cw][lane][j] = pack_f16x2(w[j], w[j]);
             }
             __syncwarp();
             uint32_t plo[JN][NW], phi[JN][NW];
@@ -388,39 +400,42 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
               for (int i = 0; i < NW; ++i) plo[j][i] = phi[j][i] = 0u;
             }
 #pragma unroll
-            for (int j2 = 0; j2 < kGKeysPerWarp; j2 += 2) {
-              uint2 wp[JN];
+            for (int jk = 0; jk < kGKeysPerWarp; ++jk) {
+              uint32_t wk[JN];
+              if constexpr (JN == G) {
+                const uint4 t4 = *reinterpret_cast<const uint4*>(&sm.wbuf[cw][jk][0]);
+                wk[0] = t4.x;
+                wk[1] = t4.y;
+                wk[2] = t4.z;
+                wk[3] = t4.w;
+              } else {
 #pragma unroll
-              for (int j = 0; j < JN; ++j) wp[j] = *reinterpret_cast<const uint2*>(&sm.wbuf[cw][j][j2]);
+                for (int j = 0; j < JN; ++j) wk[j] = sm.wbuf[cw][jk][j];
+              }
+              uint32_t vw[NW];
+              load_v_lane<D>(vbase + jk * D, lane, vw);
+              uint32_t c0[NW], c1[NW];
 #pragma unroll
-              for (int u = 0; u < 2; ++u) {
-                uint32_t vw[NW];
-                load_v_lane<D>(vbase + (j2 + u) * D, lane, vw);
-                uint32_t c0[NW], c1[NW];
+              for (int i = 0; i < NW; ++i) {
+                c0[i] = e4m3x2_to_f16x2_hw(vw[i]);
+                c1[i] = e4m3x2_to_f16x2_hw(vw[i] >> 16);
+              }
 #pragma unroll
-                for (int i = 0; i < NW; ++i) {
-                  c0[i] = e4m3x2_to_f16x2_hw(vw[i]);
-                  c1[i] = e4m3x2_to_f16x2_hw(vw[i] >> 16);
-                }
+              for (int j = 0; j < JN; ++j) {
+                if (NQ != 0 || j < nq) {
 #pragma unroll
-                for (int j = 0; j < JN; ++j) {
-                  if (NQ != 0 || j < nq) {
-                    const uint32_t wj = u ? wp[j].y : wp[j].x;
-#pragma unroll
-                    for (int i = 0; i < NW; ++i) {
-                      plo[j][i] = hfma2(wj, c0[i], plo[j][i]);
-                      phi[j][i] = hfma2(wj, c1[i], phi[j][i]);
-                    }
+                  for (int i = 0; i < NW; ++i) {
+                    plo[j][i] = hfma2(wk[j], c0[i], plo[j][i]);
+                    phi[j][i] = hfma2(wk[j], c1[i], phi[j][i]);
                   }
                 }
               }
             }
+            // A code the hardware decodes to NaN poisons the sums of every query of
+            // the lane (0 * NaN is NaN), so the first query's sums tell for all.
             uint32_t nan = 0u;
 #pragma unroll
-            for (int j = 0; j < JN; ++j) {
-#pragma unroll
-              for (int i = 0; i < NW; ++i) nan |= f16x2_nan_bits(plo[j][i]) | f16x2_nan_bits(phi[j][i]);
-            }
+            for (int i = 0; i < NW; ++i) nan |= f16x2_nan_bits(plo[0][i]) | f16x2_nan_bits(phi[0][i]);
             if (!__any_sync(0xffffffffu, nan != 0u)) {
               // plo[j][i] holds dims 4i and 4i+1 of this lane, phi[j][i] dims 4i+2 and 4i+3.
 #pragma unroll
