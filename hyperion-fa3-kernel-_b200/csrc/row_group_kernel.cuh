@@ -10,7 +10,8 @@
 // HBM traffic per query falls by the run length.  The per-(query, key) arithmetic
 // is the row kernel's (popcount score, the reference's clamped online softmax per
 // 32-key group, f16x2 products of the hardware FP8 decode with the exact redo for
-// codes 0x7F / 0xFF), with the FP8 decode of a key shared by the run's queries.
+// codes 0x7F / 0xFF), with the FP8 decode of a key shared by the run's queries,
+// and the running max moved only when a group exceeds it by more than ln 4.
 //
 // Each query keeps its own key range [0, kv_end), so a run may also hold rows of
 // one (batch, head) at different causal positions; the run streams the longest.
