@@ -215,6 +215,15 @@ def roofline_numbers(wk, pairs, kernel_ms, pk):
             "frac_of_spec": achieved / SPEC_PEAKS["bf16_tflops"], "algorithmic_flops_per_launch": flops}
 
 
+# The arithmetic each kernel computes the path in.
+DTYPES = {
+    "tile": "sign-bit QK (e4m3 +-1 MMA, exact int) / f16 PV",
+    "row": "sign-bit QK (popc, exact int) / f16x2 PV products, f32 accumulation",
+    "group": "sign-bit QK (popc, exact int) / f16x2 PV products, f32 accumulation",
+    "group_mma": "sign-bit QK (popc, exact int) / e4m3 PV MMA (V codes x weights in 3 e4m3 pieces), f32 accumulation",
+}
+
+
 def read_traffic(kernel_tag):
     """DRAM bytes per launch from the committed ncu summary, if one exists:
     a line `traffic_bytes_per_launch: <int>` in profiles/<kernel_tag>.md."""
@@ -641,8 +650,10 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
         kernel_ms = total_ms / args.steps
         roof = roofline_numbers(wk, pairs, kernel_ms, pk)
         roof["peak_source"] = pk_src
-        roof["kernel"] = f"{info['path']} kernel"
-        kernel_tag = f"{info['path'] or 'row'}_kernel_{name}"
+        kname = {"row": "row_kernel", "group": "row_group_kernel", "group_mma": "row_mma_kernel",
+                 "tile": "tile_kernel"}.get(info.get("kernel"), f"{info['path'] or 'row'}_kernel")
+        roof["kernel"] = kname
+        kernel_tag = f"{kname}_{name}"
         roof["traffic"] = read_traffic(kernel_tag)
         roof["traffic_source"] = (f"carried over from one ncu capture (profiles/{kernel_tag}.md), not measured in "
                                   "this run" if roof["traffic"] is not None else None)
@@ -657,8 +668,7 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
             "metric": METRIC, "value": value, "unit": "pairs/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms_max / args.steps, "higher_is_better": True,
             "scaling": scaling, "vs_baseline": None,
-            "dtype": "sign-bit QK (e4m3 +-1 MMA, exact int) / f16 PV" if info["path"] == "tile"
-                     else "sign-bit QK (popc, exact int) / f16x2 PV products, f32 accumulation",
+            "dtype": DTYPES.get(info.get("kernel"), DTYPES["row"]),
             "data": "synthetic: seeded random sign bits for Q/K, N(0,1) V as FP8 e4m3 with per-head scale",
             "config": workload_config(wk, desc, world, scaling),
             "launch": {"path": info["path"], "kv_splits": info["splits"], "grid": info["grid"]},

@@ -21,7 +21,7 @@ OUT = os.path.join(HERE, "hyperion_b200", "libhyperion_b200.so")
 INCLUDE = os.path.join(REPO, "include")
 
 SOURCES = ["capi.cu"]
-HEADERS = ["common.cuh", "row_kernel.cuh", "row_group_kernel.cuh", "tile_kernel.cuh", "tcgen05.cuh", "kv_write.cuh",
+HEADERS = ["common.cuh", "row_kernel.cuh", "row_group_kernel.cuh", "row_mma_kernel.cuh", "tile_kernel.cuh", "tcgen05.cuh", "kv_write.cuh",
            "launch_table.h"]
 
 NVCC_FLAGS = [

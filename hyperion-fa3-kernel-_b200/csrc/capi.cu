@@ -18,14 +18,26 @@
 #include "common.cuh"
 #include "row_kernel.cuh"
 #include "row_group_kernel.cuh"
+#include "row_mma_kernel.cuh"
 #include "tile_kernel.cuh"
 #include "kv_write.cuh"
 #include "launch_table.h"
 
 namespace {
 
+// Main kernel of a call, out[4] of hyperion_last_call_info.
+enum KernelId { kKernelNone = 0, kKernelRow = 1, kKernelGroup = 2, kKernelGroupMma = 3, kKernelTile = 4 };
+
 thread_local std::string g_last_error;
-thread_local int32_t g_last_call[4] = {0, 0, 0, 0};
+thread_local int32_t g_last_call[5] = {0, 0, 0, 0, 0};
+// Split count and workspace bytes of the last row-path call, for the message of a
+// workspace refusal.
+thread_local int g_last_splits = 1;
+thread_local size_t g_last_need = 0;
+
+void clear_last_call() {
+  for (int32_t& v : g_last_call) v = 0;
+}
 
 // A fault armed by hyperion_debug_fault for the next forward of this thread.
 struct FaultHook {
@@ -55,6 +67,8 @@ struct DevInfo {
   int tile_ctas = 0, tile_smem = 0;
   bool tile_ok = false;
   std::string tile_why;  // why the tile kernel is unavailable ("" when it is)
+  int mma_ctas = 0, mma_smem = 0;  // grouped-query kernel with the products on the tensor core
+  bool mma_ok = false;
 };
 
 constexpr int kMaxDevices = 64;
@@ -110,6 +124,11 @@ int get_dev(const DevInfo** out) {
       di.tile_why = why;
       cudaGetLastError();
     }
+    di.mma_ok = hyp::rmma::setup(di.mma_ctas, di.mma_smem) == cudaSuccess && di.mma_ctas > 0;
+    if (!di.mma_ok) {
+      di.mma_ctas = 0;
+      cudaGetLastError();
+    }
     di.ready = true;
   }
   *out = &di;
@@ -117,7 +136,8 @@ int get_dev(const DevInfo** out) {
 }
 
 // The measured split count for a call of `kernel` (0 row kernel, 1 grouped row
-// kernel with 4 query heads per KV head) with `items` work items of up to `keys`
+// kernel with 4 query heads per KV head, 2 the same on the tensor-core grouped
+// kernel) with `items` work items of up to `keys`
 // keys, or 0 when the launch table (launch_table.h, written by tune_launch.py from a
 // sweep on B200) has no entry within a factor of 2 of both, or was measured on
 // another SM count or head_dim.
@@ -157,27 +177,32 @@ int choose_splits(const DevInfo& di, int D, int total_work, long long max_keys) 
   return (int)std::max<long long>(ns, 1);
 }
 
-// KV splits per unit of the grouped row kernel, whose unit holds up to
-// group_items (at most 4) work items.  Decode with 4 query heads per KV head takes
-// the launch table's measured count near its shape; otherwise the rule: enough
+// KV splits per unit of a grouped kernel (`mma`: the one with the products on the
+// tensor core), whose unit holds up to group_items (at most 4) work items.  Decode
+// with 4 query heads per KV head takes the launch table's measured count near its
+// shape for that kernel; otherwise the rule: enough
 // units for 4 per CTA slot and, while units are scarce (fewer than 16 per slot),
-// pieces of at most 2048 keys so that ragged contexts balance; no piece shorter
+// pieces of at most 2048 keys (8192 on the tensor-core kernel) so that ragged
+// contexts balance; no piece shorter
 // than 512 keys, at most 16 pieces.  (Paged decode with 32 query heads over 8 KV
 // heads, contexts U[512, 32768]: 1.21 ms at 13-16 pieces against 1.27 ms at the row
 // kernel's choice of 4 in isolated calls; the same 1.26 ms under the sustained
 // power cap, where the whole step with host copies gains 4 %.)
 int choose_group_splits(const DevInfo& di, int D, long long items, int group_items, bool decode,
-                        long long max_keys) {
+                        long long max_keys, bool mma) {
   if (items <= 0) return 1;
   if (decode && group_items == 4) {
-    const int measured = table_splits(di, 1, D, items, max_keys);
+    const int measured = table_splits(di, mma ? 2 : 1, D, items, max_keys);
     if (measured > 0) return measured;
   }
   const long long chunks = (items + group_items - 1) / group_items;
-  const long long slots = (long long)di.n_sm * ((D == 256) ? di.group_ctas_256 : di.group_ctas_128);
+  const long long slots =
+      (long long)di.n_sm * (mma ? di.mma_ctas : (D == 256) ? di.group_ctas_256 : di.group_ctas_128);
   if (chunks >= 16 * slots) return 1;
   long long ns = (4 * slots + chunks - 1) / chunks;
-  ns = std::max(ns, (max_keys + 2047) / 2048);
+  // The tensor-core kernel pays more per piece (a TMEM read-out) and less per key.
+  const long long piece = mma ? 8192 : 2048;
+  ns = std::max(ns, (max_keys + piece - 1) / piece);
   ns = std::min(ns, std::max<long long>(1, max_keys / 512));
   ns = std::min<long long>(ns, 16);
   return (int)std::max<long long>(ns, 1);
@@ -190,12 +215,15 @@ size_t partial_bytes(int total_work, int n_split, int D) {
 
 // Workspace of the automatic split choice, for either row kernel (a forced
 // num_splits needs 256 + total_work * num_splits * (2 + head_dim) * 4 bytes).
-// The grouped kernel's choice is bounded by its smallest unit count, 4 items a unit.
+// The grouped kernels' choice is bounded by their smallest unit count, 4 items a unit.
 size_t workspace_needed(const DevInfo& di, int total_work, int D, int block_size, int num_blocks) {
   const long long max_keys = (long long)std::max(block_size, 1) * std::max(num_blocks, 1);
-  const int ns = std::max({choose_splits(di, D, total_work, max_keys),
-                           choose_group_splits(di, D, total_work, 4, true, max_keys),
-                           choose_group_splits(di, D, total_work, 4, false, max_keys)});
+  int ns = std::max({choose_splits(di, D, total_work, max_keys),
+                     choose_group_splits(di, D, total_work, 4, true, max_keys, false),
+                     choose_group_splits(di, D, total_work, 4, false, max_keys, false)});
+  if (di.mma_ok)
+    ns = std::max({ns, choose_group_splits(di, D, total_work, 4, true, max_keys, true),
+                   choose_group_splits(di, D, total_work, 4, false, max_keys, true)});
   return hyp::kWsPartials + partial_bytes(total_work, ns, D);
 }
 
@@ -203,13 +231,13 @@ size_t workspace_needed(const DevInfo& di, int total_work, int D, int block_size
 
 extern "C" {
 
-int32_t hyperion_version(void) { return 1 * 10000 + 1 * 100 + 0; }
+int32_t hyperion_version(void) { return 1 * 10000 + 2 * 100 + 0; }
 
 const char* hyperion_last_error_string(void) { return g_last_error.c_str(); }
 
 int hyperion_last_call_info(int32_t* out, int32_t n) {
   if (out == nullptr) return fail(HYPERION_ERR_INVALID_ARG, "out is NULL");
-  for (int i = 0; i < n && i < 4; ++i) out[i] = g_last_call[i];
+  for (int i = 0; i < n && i < 5; ++i) out[i] = g_last_call[i];
   return HYPERION_OK;
 }
 
@@ -224,10 +252,11 @@ int hyperion_launch_info(int32_t* out, int32_t n) {
   const DevInfo* di = nullptr;
   const int rc = get_dev(&di);
   if (rc) return rc;
-  const int32_t v[12] = {di->n_sm,           di->row_ctas_128,      di->row_smem_128,  di->tile_ctas,
+  const int32_t v[15] = {di->n_sm,           di->row_ctas_128,      di->row_smem_128,  di->tile_ctas,
                          di->tile_smem,       di->row_ctas_256,      di->tile_ok ? 1 : 0, hyp::row::kThreads,
-                         hyp::row::kGThreads, di->group_ctas_128,    di->group_smem_128, hyp::tile::kThreads};
-  for (int i = 0; i < n && i < 12; ++i) out[i] = v[i];
+                         hyp::row::kGThreads, di->group_ctas_128,    di->group_smem_128, hyp::tile::kThreads,
+                         di->mma_ok ? hyp::rmma::kThreads : 0, di->mma_ctas, di->mma_ok ? di->mma_smem : 0};
+  for (int i = 0; i < n && i < 15; ++i) out[i] = v[i];
   if (!di->tile_ok) g_last_error = "tile kernel unavailable: " + di->tile_why;
   return HYPERION_OK;
 }
@@ -253,7 +282,7 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   if (total_work == 0) {
     // Nothing to do, whatever the tensors hold: a rank that owns no (batch, head)
     // row passes empty ones.
-    g_last_call[0] = g_last_call[1] = g_last_call[2] = g_last_call[3] = 0;
+    clear_last_call();
     return HYPERION_OK;
   }
   if (ext->n_bh < 1) return fail(HYPERION_ERR_INVALID_ARG, "n_bh (context_lens numel) < 1");
@@ -338,7 +367,7 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
     g_fault.armed = false;
   }
 
-  g_last_call[0] = g_last_call[1] = g_last_call[2] = g_last_call[3] = 0;
+  clear_last_call();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const long long max_keys = (long long)block_size * num_blocks;
 
@@ -367,6 +396,7 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
     g_last_call[1] = 1;
     g_last_call[2] = 1;
     g_last_call[3] = grid;
+    g_last_call[4] = kKernelTile;
     return HYPERION_OK;
   }
 
@@ -374,14 +404,34 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   // split, and a run of them on one KV row streams its keys once: the query heads
   // of one KV head (grouped-query attention), or neighbouring query rows of one
   // (batch, head) in a prefill worklist.
+  // At head_dim 128 with a per-tensor or per-head V scale the grouped runs take the
+  // kernel with the P.V products on the tensor core (row_mma_kernel.cuh); otherwise,
+  // or when the caller asks for it, the one with the products on the CUDA cores.
   const bool grouped = kv_group > 1 || seq_q > 1;
   p.group_items = !grouped ? 1 : (kv_group > 1) ? std::min(kv_group, hyp::row::kGroupMax) : hyp::row::kGroupMax;
+  const int group_req = opt ? opt->group_kernel : HYPERION_GROUP_AUTO;
+  if (group_req != HYPERION_GROUP_AUTO && group_req != HYPERION_GROUP_CUDA && group_req != HYPERION_GROUP_MMA)
+    return fail(HYPERION_ERR_INVALID_ARG, "group_kernel must be HYPERION_GROUP_AUTO, _CUDA or _MMA");
+  CUtensorMap vmap;
+  const bool mma_fits = grouped && group_req != HYPERION_GROUP_CUDA && di->mma_ok &&
+                        hyp::rmma::fits(head_dim, p.v_scale_mode, inv_sqrt_d, block_size, num_blocks, V_cache,
+                                        ext->pool_rows) &&
+                        hyp::rmma::encode_vmap(&vmap, V_cache, ext->pool_rows, block_size);
+  if (grouped && group_req == HYPERION_GROUP_MMA && !mma_fits)
+    return fail(HYPERION_ERR_UNSUPPORTED,
+                "the tensor-core grouped kernel needs head_dim 128, a per-tensor or per-head V scale, "
+                "|inv_sqrt_d| <= 0.117, one page per row or pages of 8 to 128 keys dividing 128 or of a multiple of "
+                "128 keys, a "
+                "16-byte aligned V_cache of fewer than 2^32 rows, and a device that loaded it");
+  const bool use_mma = mma_fits;
   const long long chunks = ((long long)total_work + p.group_items - 1) / p.group_items;
   int ns = (opt && opt->num_splits > 0) ? std::min(opt->num_splits, 16)
            : grouped                    ? choose_group_splits(*di, head_dim, total_work, p.group_items, seq_q == 1,
-                                                                  max_keys)
+                                                                  max_keys, use_mma)
                                         : choose_splits(*di, head_dim, total_work, max_keys);
   const size_t need = hyp::kWsPartials + partial_bytes(total_work, ns, head_dim);
+  g_last_splits = ns;
+  g_last_need = need;
   if (workspace_bytes < need) return fail(HYPERION_ERR_WORKSPACE, "workspace smaller than hyperion_workspace_bytes()");
   p.n_split = ns;
   const long long units = (long long)total_work * ns;
@@ -390,7 +440,14 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   e = cudaMemsetAsync(ws + hyp::kWsCounters, 0, 64, st);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(counters)");
   int grid = 0;
-  if (grouped) {
+  int kernel = kKernelRow;
+  if (use_mma) {
+    const long long gunits = chunks * ns;
+    grid = (int)std::min<long long>(gunits, (long long)sm_use * di->mma_ctas);
+    hyp::rmma::row_mma_kernel<<<grid, hyp::rmma::kThreads, di->mma_smem, st>>>(p, (int)gunits, vmap);
+    kernel = kKernelGroupMma;
+  } else if (grouped) {
+    kernel = kKernelGroup;
     const long long gunits = chunks * ns;
     const int ctas = (head_dim == 256) ? di->group_ctas_256 : di->group_ctas_128;
     const int smem = (head_dim == 256) ? di->group_smem_256 : di->group_smem_128;
@@ -425,6 +482,7 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   g_last_call[1] = ns;
   g_last_call[2] = ns > 1 ? 2 : 1;
   g_last_call[3] = grid;
+  g_last_call[4] = kernel;
   return HYPERION_OK;
 }
 
@@ -582,19 +640,14 @@ extern "C" int hyperion_apex_kernel_noalloc(const int32_t* worklist, int32_t tot
                                          num_blocks, inv_sqrt_d, causal, ext, nullptr, scratch,
                                          HYPERION_NOALLOC_SCRATCH_BYTES, stream);
   if (rc == HYPERION_ERR_WORKSPACE) {
-    const DevInfo* di = nullptr;
-    if (get_dev(&di) != HYPERION_OK) return rc;
-    const long long max_keys = (long long)block_size * num_blocks;
-    // The split count the forward chose: a query row per (batch, head) takes the
-    // row kernel, several take the grouped kernel (4 work items a unit).
-    const int ns = (seq_q > 1) ? choose_group_splits(*di, head_dim, total_work, 4, false, max_keys)
-                               : choose_splits(*di, head_dim, total_work, max_keys);
+    // The split count and scratch the forward worked out before it refused.
+    const int ns = g_last_splits;
     char msg[320];
     std::snprintf(msg, sizeof(msg),
                   "hyperion_apex_kernel_noalloc: this call needs %zu bytes of scratch (%d work items x %d KV splits "
                   "of %d floats), more than its fixed %zu bytes; pass fewer work items per call or use "
                   "hyperion_apex_kernel with a workspace",
-                  (size_t)hyp::kWsPartials + partial_bytes(total_work, ns, head_dim), (int)total_work, ns,
+                  g_last_need, (int)total_work, ns,
                   2 + (int)head_dim, (size_t)HYPERION_NOALLOC_SCRATCH_BYTES);
     g_last_error = msg;
   }

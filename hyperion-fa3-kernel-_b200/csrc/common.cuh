@@ -106,6 +106,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete sleeps
+// in the barrier unit until it completes or about `ns` nanoseconds pass, instead
+// of returning at once and spinning in the issue slots the working warps need.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+// Longest sleep of one try in a bounded wait: well under the shortest bound a
+// test sets (about a millisecond), so a wait that runs out still ends promptly.
+constexpr uint32_t kWaitSleepNs = 100000;
+
 // Abort flag and wait bound of a CTA, kept in its shared memory: the flag is set
 // by the first wait that runs out, and every other wait then gives up.
 struct WaitCtl {
@@ -120,7 +136,7 @@ __device__ __noinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, vola
   const long long t0 = clock64();
   const long long limit = ctl->limit;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, kWaitSleepNs)) return true;
     if (ctl->flag) return false;
     if (clock64() - t0 > limit) {
       raise_error(err, HYPERION_DEVERR_WAIT_TIMEOUT);

@@ -83,6 +83,174 @@ struct GroupSmem {
 template <int D>
 constexpr int group_ctas() { return D == 128 ? 10 : 5; }
 
+// The producer warp of the grouped kernels.  It takes unit tickets, cuts each
+// unit (up to kGroupMax work items, one KV split) into runs of consecutive items on
+// one KV row, publishes each run in a 2-slot ring (run_full / run_empty) and hands
+// the run's key range of its split, [k_lo, k_hi) on KV row kv, to
+// stream(kv, k_lo, k_hi), which loads its stages and returns false when a wait gave
+// up.  A split starts at a multiple of key_round keys.
+template <int W, class SM, class Stream>
+__device__ __forceinline__ void group_producer(const FwdParams& p, SM& sm, int total_units, int key_round,
+                                               volatile WaitCtl* abort, Stream&& stream) {
+  const int lane = threadIdx.x & 31;
+  uint32_t rc = 0;  // run slots published
+  bool aborted = false;
+  for (;;) {
+    int t = 0;
+    if (lane == 0) t = (int)atomicAdd(&p.counters[0], 1u);
+    t = __shfl_sync(0xffffffffu, t, 0);
+    if (t >= total_units) {
+      const int us = rc & 1;
+      if (!mbar_wait_warp(&sm.run_empty[us], ((rc >> 1) & 1) ^ 1, abort, p.err)) break;
+      if (lane == 0) {
+        sm.slot[us].unit = -1;
+        mbar_arrive(&sm.run_full[us]);
+      }
+      ++rc;
+      break;
+    }
+    const int unit = t;
+    const int chunk = unit / p.n_split;
+    const int split = unit - chunk * p.n_split;
+    const int i0 = chunk * p.group_items;
+    const int n = min(p.group_items, p.total_work - i0);
+    // Lane j < n resolves item i0 + j.
+    ItemInfo inf;
+    inf.bh = 0;
+    inf.q_idx = 0;
+    inf.kv_end = 0;
+    inf.valid = false;
+    if (lane < n) {
+      inf = resolve_item(p, i0 + lane);
+      if (split == 0) check_item_errors(p, i0 + lane);
+    }
+    const int kvb = (lane < n && inf.valid) ? kv_of(p, inf.bh) : -1;
+    int r = 0;
+    while (r < n) {
+      const int kv_r = __shfl_sync(0xffffffffu, kvb, r);
+      if (kv_r < 0) {  // a bad item: flagged above, not written
+        ++r;
+        continue;
+      }
+      const unsigned diff = __ballot_sync(0xffffffffu, lane > r && lane < n && kvb != kv_r);
+      const int e = diff ? (__ffs(diff) - 1) : n;
+      const bool in_run = lane >= r && lane < e;
+      const int maxend = __reduce_max_sync(0xffffffffu, in_run ? inf.kv_end : 0);
+      int chunk_k = (maxend + p.n_split - 1) / p.n_split;
+      chunk_k = (chunk_k + key_round - 1) / key_round * key_round;
+      const int k_lo = min(split * chunk_k, maxend);
+      const int k_hi = min(k_lo + chunk_k, maxend);
+      const int bh_r = __shfl_sync(0xffffffffu, inf.bh, r);
+
+      const int us = rc & 1;
+      if (!mbar_wait_warp(&sm.run_empty[us], ((rc >> 1) & 1) ^ 1, abort, p.err)) {
+        aborted = true;
+        break;
+      }
+      RunSlot<W>& sl = sm.slot[us];
+      if (in_run) {
+        const int j = lane - r;
+        sl.item[j] = i0 + lane;
+        sl.orow[j] = inf.bh * p.seq_q + inf.q_idx;
+        sl.kv_end[j] = inf.kv_end;
+        const uint32_t* qrow = p.q + ((long long)inf.bh * p.seq_q + inf.q_idx) * W;
+#pragma unroll
+        for (int i = 0; i < W; ++i) sl.q[j][i] = __ldg(qrow + i);
+      }
+      if (lane == 0) {
+        sl.unit = unit;
+        sl.split = split;
+        sl.nq = e - r;
+        sl.bh0 = bh_r;
+        sl.kv = kv_r;
+        sl.k_lo = k_lo;
+        sl.k_hi = k_hi;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.run_full[us]);
+      ++rc;
+
+      if (!stream(kv_r, k_lo, k_hi)) {
+        aborted = true;
+        break;
+      }
+      r = e;
+    }
+    if (aborted) break;
+  }
+}
+
+// The grouped row kernel's stages: 64 keys each, sign bits to sm.k and FP8 codes to
+// sm.v by bulk copies per page piece, the key count and valid-key mask to sm.hdr,
+// through the NS-stage ring full / empty.  `it` counts the stages armed.
+template <int D, int NS, class SM>
+__device__ __forceinline__ bool group_stream(const FwdParams& p, SM& sm, uint32_t& it, int kv_r, int k_lo, int k_hi,
+                                             uint64_t pol, volatile WaitCtl* abort) {
+  constexpr int W = D / 32;
+  const int lane = threadIdx.x & 31;
+  for (int k0 = k_lo; k0 < k_hi; k0 += kKeysPerStage) {
+    const int s = it % NS;
+    if (!mbar_wait_warp(&sm.empty[s], ((it / NS) & 1) ^ 1, abort, p.err)) return false;
+    const int nk = min(kKeysPerStage, k_hi - k0);
+    const int bs = p.block_size;
+    const int p0 = k0 / bs;
+    const int np = (k0 + nk - 1) / bs - p0 + 1;
+    uint32_t bytes = 0;
+    unsigned long long mask = 0ull;
+    for (int i = lane; i < np; i += 32) {
+      const int page = p0 + i;
+      const int lo = max(k0, page * bs);
+      const int hi = min(k0 + nk, (page + 1) * bs);
+      const long long id = page_block_id_kv(p, kv_r, page);
+      if (id >= 0) {
+        bytes += (uint32_t)(hi - lo) * (uint32_t)(W * 4 + D);
+        const int a = lo - k0, b = hi - k0;
+        const unsigned long long bits = (b - a >= 64) ? ~0ull : ((1ull << (b - a)) - 1ull);
+        mask |= bits << a;
+      } else {
+        raise_error(p.err, HYPERION_DEVERR_BAD_BLOCK);
+      }
+    }
+    bytes = __reduce_add_sync(0xffffffffu, bytes);
+    mask = ((unsigned long long)__reduce_or_sync(0xffffffffu, (uint32_t)(mask >> 32)) << 32) |
+           __reduce_or_sync(0xffffffffu, (uint32_t)mask);
+    // Test hook: the stage numbered fault_stage is left unarmed, with no copy
+    // in flight on it, so the consumers' wait for it runs out.
+    const bool armed = (int)it != p.fault_stage;
+    if (lane == 0 && armed) {
+      sm.hdr[s].nkeys = nk;
+      sm.hdr[s].mask = mask;
+      if (bytes) {
+        mbar_arrive_expect_tx(&sm.full[s], bytes);
+      } else {
+        mbar_arrive(&sm.full[s]);
+      }
+    }
+    __syncwarp();
+    for (int i = lane; armed && i < np; i += 32) {
+      const int page = p0 + i;
+      const int lo = max(k0, page * bs);
+      const int hi = min(k0 + nk, (page + 1) * bs);
+      const long long id = page_block_id_kv(p, kv_r, page);
+      if (id >= 0) {
+        const long long slot0 = id * bs + (lo - page * bs);
+        const uint32_t cnt = (uint32_t)(hi - lo);
+        bulk_g2s_stream(&sm.k[s][(lo - k0) * W * 4], p.k + slot0 * W, cnt * W * 4, &sm.full[s], pol);
+        bulk_g2s_stream(&sm.v[s][(lo - k0) * D], p.v + slot0 * D, cnt * D, &sm.full[s], pol);
+      }
+    }
+    ++it;
+  }
+  return true;
+}
+
+// On the way out of an aborted CTA: let the copies of the last (up to NS) armed
+// stages land before the CTA's shared memory is released.
+template <int NS>
+__device__ __forceinline__ void drain_stages(uint64_t* full, uint32_t it, long long limit) {
+  for (uint32_t i = (it > (uint32_t)NS ? it - NS : 0u); i < it; ++i) mbar_drain(&full[i % NS], (i / NS) & 1, limit);
+}
+
 template <int D>
 __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(FwdParams p, int total_units) {
   constexpr int W = D / 32;
@@ -126,149 +294,10 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
     // ------------------------------------------------------------ producer
     const uint64_t pol = policy_evict_first();
     uint32_t it = 0;  // stages armed
-    uint32_t rc = 0;  // run slots published
-    bool aborted = false;
-    for (;;) {
-      int t = 0;
-      if (lane == 0) t = (int)atomicAdd(&p.counters[0], 1u);
-      t = __shfl_sync(0xffffffffu, t, 0);
-      if (t >= total_units) {
-        const int us = rc & 1;
-        if (!mbar_wait_warp(&sm.run_empty[us], ((rc >> 1) & 1) ^ 1, abort, p.err)) break;
-        if (lane == 0) {
-          sm.slot[us].unit = -1;
-          mbar_arrive(&sm.run_full[us]);
-        }
-        ++rc;
-        break;
-      }
-      const int unit = t;
-      const int chunk = unit / p.n_split;
-      const int split = unit - chunk * p.n_split;
-      const int i0 = chunk * p.group_items;
-      const int n = min(p.group_items, p.total_work - i0);
-      // Lane j < n resolves item i0 + j.
-      ItemInfo inf;
-      inf.bh = 0;
-      inf.q_idx = 0;
-      inf.kv_end = 0;
-      inf.valid = false;
-      if (lane < n) {
-        inf = resolve_item(p, i0 + lane);
-        if (split == 0) check_item_errors(p, i0 + lane);
-      }
-      const int kvb = (lane < n && inf.valid) ? kv_of(p, inf.bh) : -1;
-      int r = 0;
-      while (r < n) {
-        const int kv_r = __shfl_sync(0xffffffffu, kvb, r);
-        if (kv_r < 0) {  // a bad item: flagged above, not written
-          ++r;
-          continue;
-        }
-        const unsigned diff = __ballot_sync(0xffffffffu, lane > r && lane < n && kvb != kv_r);
-        const int e = diff ? (__ffs(diff) - 1) : n;
-        const bool in_run = lane >= r && lane < e;
-        const int maxend = __reduce_max_sync(0xffffffffu, in_run ? inf.kv_end : 0);
-        int chunk_k = (maxend + p.n_split - 1) / p.n_split;
-        chunk_k = (chunk_k + 15) & ~15;
-        const int k_lo = min(split * chunk_k, maxend);
-        const int k_hi = min(k_lo + chunk_k, maxend);
-        const int bh_r = __shfl_sync(0xffffffffu, inf.bh, r);
-
-        const int us = rc & 1;
-        if (!mbar_wait_warp(&sm.run_empty[us], ((rc >> 1) & 1) ^ 1, abort, p.err)) {
-          aborted = true;
-          break;
-        }
-        RunSlot<W>& sl = sm.slot[us];
-        if (in_run) {
-          const int j = lane - r;
-          sl.item[j] = i0 + lane;
-          sl.orow[j] = inf.bh * p.seq_q + inf.q_idx;
-          sl.kv_end[j] = inf.kv_end;
-          const uint32_t* qrow = p.q + ((long long)inf.bh * p.seq_q + inf.q_idx) * W;
-#pragma unroll
-          for (int i = 0; i < W; ++i) sl.q[j][i] = __ldg(qrow + i);
-        }
-        if (lane == 0) {
-          sl.unit = unit;
-          sl.split = split;
-          sl.nq = e - r;
-          sl.bh0 = bh_r;
-          sl.kv = kv_r;
-          sl.k_lo = k_lo;
-          sl.k_hi = k_hi;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.run_full[us]);
-        ++rc;
-
-        for (int k0 = k_lo; k0 < k_hi; k0 += kKeysPerStage) {
-          const int s = it % kGStages;
-          if (!mbar_wait_warp(&sm.empty[s], ((it / kGStages) & 1) ^ 1, abort, p.err)) {
-            aborted = true;
-            break;
-          }
-          const int nk = min(kKeysPerStage, k_hi - k0);
-          const int bs = p.block_size;
-          const int p0 = k0 / bs;
-          const int np = (k0 + nk - 1) / bs - p0 + 1;
-          uint32_t bytes = 0;
-          unsigned long long mask = 0ull;
-          for (int i = lane; i < np; i += 32) {
-            const int page = p0 + i;
-            const int lo = max(k0, page * bs);
-            const int hi = min(k0 + nk, (page + 1) * bs);
-            const long long id = page_block_id_kv(p, kv_r, page);
-            if (id >= 0) {
-              bytes += (uint32_t)(hi - lo) * (uint32_t)(W * 4 + D);
-              const int a = lo - k0, b = hi - k0;
-              const unsigned long long bits = (b - a >= 64) ? ~0ull : ((1ull << (b - a)) - 1ull);
-              mask |= bits << a;
-            } else {
-              raise_error(p.err, HYPERION_DEVERR_BAD_BLOCK);
-            }
-          }
-          bytes = __reduce_add_sync(0xffffffffu, bytes);
-          mask = ((unsigned long long)__reduce_or_sync(0xffffffffu, (uint32_t)(mask >> 32)) << 32) |
-                 __reduce_or_sync(0xffffffffu, (uint32_t)mask);
-          // Test hook: the stage numbered fault_stage is left unarmed, with no copy
-          // in flight on it, so the consumers' wait for it runs out.
-          const bool armed = (int)it != p.fault_stage;
-          if (lane == 0 && armed) {
-            sm.hdr[s].nkeys = nk;
-            sm.hdr[s].mask = mask;
-            if (bytes) {
-              mbar_arrive_expect_tx(&sm.full[s], bytes);
-            } else {
-              mbar_arrive(&sm.full[s]);
-            }
-          }
-          __syncwarp();
-          for (int i = lane; armed && i < np; i += 32) {
-            const int page = p0 + i;
-            const int lo = max(k0, page * bs);
-            const int hi = min(k0 + nk, (page + 1) * bs);
-            const long long id = page_block_id_kv(p, kv_r, page);
-            if (id >= 0) {
-              const long long slot0 = id * bs + (lo - page * bs);
-              const uint32_t cnt = (uint32_t)(hi - lo);
-              bulk_g2s_stream(&sm.k[s][(lo - k0) * W * 4], p.k + slot0 * W, cnt * W * 4, &sm.full[s], pol);
-              bulk_g2s_stream(&sm.v[s][(lo - k0) * D], p.v + slot0 * D, cnt * D, &sm.full[s], pol);
-            }
-          }
-          ++it;
-        }
-        if (aborted) break;
-        r = e;
-      }
-      if (aborted) break;
-    }
-    if (abort->flag && lane == 0) {
-      // Let the copies of the last (up to kGStages) armed stages land before exit.
-      for (uint32_t i = (it > (uint32_t)kGStages ? it - kGStages : 0u); i < it; ++i)
-        mbar_drain(&sm.full[i % kGStages], (i / kGStages) & 1, p.wait_cycles);
-    }
+    group_producer<W>(p, sm, total_units, 16, abort, [&](int kv_r, int k_lo, int k_hi) {
+      return group_stream<D, kGStages>(p, sm, it, kv_r, k_lo, k_hi, pol, abort);
+    });
+    if (abort->flag && lane == 0) drain_stages<kGStages>(sm.full, it, p.wait_cycles);
   } else {
     // ------------------------------------------------------------ consumers
     const int cw = warp - 1;

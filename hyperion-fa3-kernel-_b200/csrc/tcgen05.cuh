@@ -127,6 +127,9 @@ constexpr uint32_t kIdescQK = instr_desc(0, 0, 0, 0, 128, 128);
 constexpr uint32_t kIdescQK64 = instr_desc(0, 0, 0, 0, 64, 128);
 // PV: f16 (A = P from TMEM) x f16 (B = V, MN-major: dims contiguous), 128 x 128.
 constexpr uint32_t kIdescPV = instr_desc(0, 0, 0, 1, 128, 128);
+// Grouped decode, O^T = V^T P^T: e4m3 A = V^T (M = 128 dims, MN-major: dims
+// contiguous) x e4m3 B = P^T (N = 48 weight columns, K-major: keys contiguous).
+constexpr uint32_t kIdescOT8 = instr_desc(0, 0, 1, 0, 48, 128);
 
 }  // namespace tc
 }  // namespace hyp

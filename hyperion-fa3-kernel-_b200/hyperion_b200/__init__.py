@@ -52,10 +52,12 @@ from ._capi import (  # noqa: F401
 )
 
 HYPERION_LOADED = True
-__version__ = "1.1.0"
+__version__ = "1.2.0"
 
 _O_DTYPES = {torch.float16: _capi.DTYPE_F16, torch.bfloat16: _capi.DTYPE_BF16, torch.float32: _capi.DTYPE_F32}
 _PATHS = {"auto": _capi.PATH_AUTO, "row": _capi.PATH_ROW, "tile": _capi.PATH_TILE}
+_GROUP_KERNELS = {"auto": 0, "cuda": 1, "mma": 2}
+_KERNELS = {1: "row", 2: "group", 3: "group_mma", 4: "tile"}
 
 _ws_lock = threading.Lock()
 _workspaces: dict = {}
@@ -125,6 +127,7 @@ def hyperion_apex_kernel(
     debug_scores: Optional[torch.Tensor] = None,
     kv_group: int = 1,
     sm_budget: int = 0,
+    group_kernel: str = "auto",
 ) -> None:
     """Enqueues the forward on the current CUDA stream of O's device (asynchronous).
 
@@ -141,6 +144,10 @@ def hyperion_apex_kernel(
 
     `sm_budget` (0: all): SMs the persistent kernels may occupy, for a caller that
     overlaps a collective on another stream with the forward.
+
+    `group_kernel` ("auto", "cuda" or "mma"): the kernel of the row path's grouped
+    runs (kv_group > 1 or seq_q > 1): the P.V products on the tensor core where it
+    applies (head_dim 128, a per-tensor or per-head V scale), else on the CUDA cores.
     """
     total_work = int(total_work)
     _check(int(kv_group) >= 1, "kv_group must be >= 1")
@@ -182,6 +189,7 @@ def hyperion_apex_kernel(
                and debug_scores.is_contiguous() and debug_scores.size(0) >= total_work,
                "debug_scores must be a contiguous int32 CUDA tensor [>= total_work, L]")
     _check(path in _PATHS, f"path must be one of {sorted(_PATHS)}")
+    _check(group_kernel in _GROUP_KERNELS, f"group_kernel must be one of {sorted(_GROUP_KERNELS)}")
 
     def _hint(x, i=0):
         if x is None:
@@ -194,7 +202,8 @@ def hyperion_apex_kernel(
                         _hint(grid), _hint(block), _hint(shared))
     opt = _capi.Options(_PATHS[path], int(num_splits),
                         debug_scores.data_ptr() if debug_scores is not None else None,
-                        debug_scores.size(1) if debug_scores is not None else 0, int(kv_group), int(sm_budget))
+                        debug_scores.size(1) if debug_scores is not None else 0, int(kv_group), int(sm_budget),
+                        _GROUP_KERNELS[group_kernel])
     with torch.cuda.device(dev):
         need = _capi.lib.hyperion_workspace_bytes(total_work, head_dim, block_size, num_blocks)
         _check(need > 0, f"hyperion_workspace_bytes failed: {_capi.last_error()}")
@@ -304,7 +313,8 @@ def launch_info() -> dict:
     """Launch facts derived from the current device (SM count, CTAs per SM, shared memory)."""
     keys = ("sm_count", "row_ctas_per_sm", "row_smem_bytes", "tile_ctas_per_sm", "tile_smem_bytes",
             "row_ctas_per_sm_d256", "tile_available", "row_threads", "group_threads", "group_ctas_per_sm",
-            "group_smem_bytes", "tile_threads")
+            "group_smem_bytes", "tile_threads", "group_mma_threads", "group_mma_ctas_per_sm",
+            "group_mma_smem_bytes")
     out = (ctypes.c_int32 * len(keys))()
     rc = _capi.lib.hyperion_launch_info(out, len(keys))
     if rc != _capi.HYPERION_OK:
@@ -314,11 +324,13 @@ def launch_info() -> dict:
 
 def last_call_info() -> dict:
     """What the last forward on this thread launched: path ('row' / 'tile' / None),
-    KV splits per item, number of kernels and the main kernel's grid."""
-    out = (ctypes.c_int32 * 4)()
-    _capi.lib.hyperion_last_call_info(out, 4)
+    KV splits per item, number of kernels, the main kernel's grid and the main
+    kernel ('row', 'group' on the CUDA cores, 'group_mma' on the tensor core, 'tile'
+    or None)."""
+    out = (ctypes.c_int32 * 5)()
+    _capi.lib.hyperion_last_call_info(out, 5)
     path = {_capi.PATH_ROW: "row", _capi.PATH_TILE: "tile"}.get(out[0])
-    return {"path": path, "splits": out[1], "kernels": out[2], "grid": out[3]}
+    return {"path": path, "splits": out[1], "kernels": out[2], "grid": out[3], "kernel": _KERNELS.get(out[4])}
 
 
 def library_path() -> str:

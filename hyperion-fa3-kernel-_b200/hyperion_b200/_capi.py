@@ -74,6 +74,7 @@ class Options(ctypes.Structure):
         ("debug_ld", ctypes.c_int64),
         ("kv_group", ctypes.c_int32),
         ("sm_budget", ctypes.c_int32),
+        ("group_kernel", ctypes.c_int32),
     ]
 
 

@@ -57,21 +57,26 @@ def build_worklist(q_lens: torch.Tensor, n_heads: int, kv_signatures: Optional[S
     return wl
 
 
-def launch_config(device=None, seq_q: int = 1) -> Tuple[Tuple[int, int, int], Tuple[int, int, int], int]:
+def launch_config(device=None, seq_q: int = 1, kv_group: int = 1,
+                  head_dim: int = 128) -> Tuple[Tuple[int, int, int], Tuple[int, int, int], int]:
     """(grid, block, shared) of the kernel the forward launches for `seq_q` query rows per
-    (batch, head), as the library sized it on `device`: the row kernel for decode
-    (seq_q 1), the tcgen05 tile kernel for prefill (seq_q >= 64) -- its resident
-    CTAs, its block size and its dynamic shared memory.  The forward treats the
-    triple it is given as a hint only."""
+    (batch, head) and `kv_group` query heads per KV head, as the library sized it on
+    `device`: the row kernel for decode (seq_q 1), the grouped kernel for grouped-query
+    decode or short prefill rows (on the tensor core at head_dim 128), the tcgen05
+    tile kernel for prefill (seq_q >= 64) -- its resident CTAs, its block size and its
+    dynamic shared memory.  The forward treats the triple it is given as a hint only."""
     from . import launch_info
 
     dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index)
     with torch.cuda.device(dev):
         info = launch_info()
-    if seq_q >= 64 and info["tile_available"]:
+    if seq_q >= 64 and info["tile_available"] and head_dim == 128:
         return (info["sm_count"] * info["tile_ctas_per_sm"], 1, 1), (info["tile_threads"], 1, 1), \
             int(info["tile_smem_bytes"])
-    if seq_q > 1:
+    if (seq_q > 1 or kv_group > 1) and head_dim == 128 and info["group_mma_threads"]:
+        return (info["sm_count"] * info["group_mma_ctas_per_sm"], 1, 1), (info["group_mma_threads"], 1, 1), \
+            int(info["group_mma_smem_bytes"])
+    if seq_q > 1 or kv_group > 1:
         return (info["sm_count"] * info["group_ctas_per_sm"], 1, 1), (info["group_threads"], 1, 1), \
             int(info["group_smem_bytes"])
     return (info["sm_count"] * info["row_ctas_per_sm"], 1, 1), (info["row_threads"], 1, 1), \

@@ -6,9 +6,11 @@ For decode (one query row per (batch, head)) the forward splits each row's keys
 into n pieces so that the persistent grid has enough units; the pieces are merged
 by a second kernel.  Too few pieces leave SMs idle, too many pay for partials and
 merges.  This script times every candidate split count on a grid of shapes --
-query rows x keys, for the row kernel (no grouped-query heads) and the grouped row
-kernel (4 query heads per KV head) -- with CUDA events on the launch stream, the L2
-flushed before each timed call, and keeps the fastest.  It writes
+query rows x keys, for the row kernel (no grouped-query heads) and the two grouped
+kernels (4 query heads per KV head; the P.V products on the CUDA cores or on the
+tensor core) -- with CUDA events on the launch stream, the L2 flushed before each
+timed call, and keeps the fastest.  `--kernels 2` re-measures only the listed
+kernels and keeps the table's other rows.  It writes
 
   csrc/launch_table.h   the table the library's split choice reads (rebuild after);
   --out-md FILE         a summary of the sweep (default: print to stdout).
@@ -52,14 +54,20 @@ def make_decode(n_items: int, keys: int, kv_group: int, dev) -> dict:
                 o=torch.empty(n_kv * kv_group, 128, dtype=torch.bfloat16, device=dev))
 
 
-def time_call(hyperion, w: dict, splits: int, reps: int, flush: torch.Tensor) -> float:
+# kernel id -> (query heads per KV head, the forward's group_kernel)
+KERNELS = {0: (1, "auto"), 1: (4, "cuda"), 2: (4, "mma")}
+KERNEL_NAMES = {0: "row", 1: "grouped, CUDA cores (4 heads / KV head)", 2: "grouped, tensor core (4 heads / KV head)"}
+
+
+def time_call(hyperion, w: dict, splits: int, reps: int, flush: torch.Tensor, group_kernel: str = "auto") -> float:
     """Median ms of `reps` calls with `splits` pieces per row (0: the library's choice)."""
     st = torch.cuda.current_stream()
 
     def call():
         hyperion.hyperion_apex_kernel(w["worklist"], w["worklist"].shape[0], w["q"], None, w["k"], None, w["v"],
                                       w["v_scale"], w["ctx"], w["bt"], w["o"], 1, 128, 16, w["keys"], 1,
-                                      0.088, False, path="row", num_splits=splits, kv_group=w["kv_group"])
+                                      0.088, False, path="row", num_splits=splits, kv_group=w["kv_group"],
+                                      group_kernel=group_kernel)
 
     call()
     times = []
@@ -74,24 +82,25 @@ def time_call(hyperion, w: dict, splits: int, reps: int, flush: torch.Tensor) ->
     return statistics.median(times)
 
 
-def sweep(hyperion, quick: bool):
+def sweep(hyperion, quick: bool, kernels=(0, 1, 2)):
     dev = torch.device("cuda", 0)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     reps = 3 if quick else 7
     rows = []
-    for kernel, kv_group in ((0, 1), (1, 4)):
+    for kernel in kernels:
+        kv_group, group_kernel = KERNELS[kernel]
         for n in ITEMS:
             for keys in KEYS:
                 if n * keys * 144 / kv_group > MAX_KV_BYTES:
                     continue
                 w = make_decode(n, keys, kv_group, dev)
-                auto = time_call(hyperion, w, 0, reps, flush)
+                auto = time_call(hyperion, w, 0, reps, flush, group_kernel)
                 auto_splits = hyperion.last_call_info()["splits"]
                 best = None
                 for s in CANDIDATES:
                     if s > 1 and keys // s < 256:
                         continue
-                    t = time_call(hyperion, w, s, reps, flush)
+                    t = time_call(hyperion, w, s, reps, flush, group_kernel)
                     if best is None or t < best[1]:
                         best = (s, t)
                 rows.append(dict(kernel=kernel, kv_group=kv_group, items=n, keys=keys, best=best[0], best_ms=best[1],
@@ -101,13 +110,30 @@ def sweep(hyperion, quick: bool):
     return rows
 
 
+def read_header(path: str):
+    """The rows of an existing table (with the timings its comments record)."""
+    import re
+    rows = []
+    if not os.path.exists(path):
+        return rows
+    pat = re.compile(r"\{(\d+), (\d+), (\d+), (\d+)\},\s*// ([0-9.]+) ms; the rule's (\d+): ([0-9.]+) ms")
+    for line in open(path):
+        m = pat.search(line)
+        if m:
+            k, n, keys, best, best_ms, rule, rule_ms = m.groups()
+            rows.append(dict(kernel=int(k), kv_group=KERNELS[int(k)][0], items=int(n), keys=int(keys),
+                             best=int(best), best_ms=float(best_ms), rule=int(rule), rule_ms=float(rule_ms)))
+    return rows
+
+
 def write_header(rows, sm_count: int, path: str):
     lines = [
         "// launch_table.h -- KV pieces per work item of the row kernels, measured on B200.",
         "//",
         "// Generated by tune_launch.py, which timed every candidate split count on a grid",
         "// of decode shapes (query rows x keys per row; kernel 0: row kernel, 1: grouped",
-        "// row kernel with 4 query heads per KV head; head_dim 128) and kept the fastest.",
+        "// row kernel with 4 query heads per KV head, 2: the grouped kernel with the P.V",
+        "// products on the tensor core; head_dim 128) and kept the fastest.",
         "// The library uses an entry for a call within a factor of 2 of its shape on a",
         "// device with kSplitTableSms SMs, and its occupancy-based rule otherwise.",
         "#pragma once",
@@ -116,7 +142,7 @@ def write_header(rows, sm_count: int, path: str):
         "namespace table {",
         "",
         "struct SplitEntry {",
-        "  int kernel;  // 0 row kernel, 1 grouped row kernel",
+        "  int kernel;  // 0 row kernel, 1 grouped row kernel, 2 tensor-core grouped kernel",
         "  int items;   // work items (query rows) of the call",
         "  int keys;    // keys per row (block_size * num_blocks)",
         "  int splits;  // fastest KV pieces per work item",
@@ -139,7 +165,7 @@ def summary(rows, sm_count: int) -> str:
            "| kernel | query rows | keys | best splits | best ms | rule splits | rule ms | rule / best |",
            "|---|---|---|---|---|---|---|---|"]
     for r in rows:
-        out.append(f"| {'grouped (4 heads / KV head)' if r['kernel'] else 'row'} | {r['items']} | {r['keys']} | "
+        out.append(f"| {KERNEL_NAMES[r['kernel']]} | {r['items']} | {r['keys']} | "
                    f"{r['best']} | {r['best_ms']:.4f} | {r['rule']} | {r['rule_ms']:.4f} | "
                    f"{r['rule_ms'] / r['best_ms']:.3f} |")
     return "\n".join(out) + "\n"
@@ -150,11 +176,14 @@ def main():
     ap.add_argument("--quick", action="store_true")
     ap.add_argument("--out-md", default=None)
     ap.add_argument("--header", default=os.path.join(HERE, "csrc", "launch_table.h"))
+    ap.add_argument("--kernels", default="0,1,2", help="kernel ids to measure; the table keeps the others' rows")
     a = ap.parse_args()
     import hyperion_b200 as hyperion
 
     sm_count = torch.cuda.get_device_properties(0).multi_processor_count
-    rows = sweep(hyperion, a.quick)
+    kernels = tuple(int(k) for k in a.kernels.split(","))
+    kept = [r for r in read_header(a.header) if r["kernel"] not in kernels]
+    rows = sorted(kept + sweep(hyperion, a.quick, kernels), key=lambda r: (r["kernel"], r["items"], r["keys"]))
     write_header(rows, sm_count, a.header)
     text = summary(rows, sm_count)
     if a.out_md:

@@ -80,6 +80,14 @@ extern "C" {
 #define HYPERION_PATH_ROW    1  /* split-KV row kernel (CUDA cores, HBM streaming): any input */
 #define HYPERION_PATH_TILE   2  /* 128-row tcgen05 tile kernel: head_dim 128, non per-slot V scale */
 
+/* Kernel of the row path's grouped runs (kv_group > 1, or seq_q > 1): */
+#define HYPERION_GROUP_AUTO  0  /* the tensor-core kernel where it applies, else the CUDA-core one */
+#define HYPERION_GROUP_CUDA  1  /* products w * v on the CUDA cores: any input */
+#define HYPERION_GROUP_MMA   2  /* products on tcgen05 (O^T = V^T P^T): head_dim 128, a per-tensor or
+                                   per-head V scale, |inv_sqrt_d| <= 0.117, num_blocks 1 or a
+                                   block_size of 8..128 dividing 128 or a multiple of 128, and a
+                                   16-byte aligned V_cache */
+
 typedef struct hyperion_extents {
   int32_t n_bh;               /* numel of context_lens: number of (batch, head) rows (KV rows under kv_group) */
   int64_t pool_rows;          /* rows of K_cache and of V_cache */
@@ -112,6 +120,8 @@ typedef struct hyperion_options {
                             on another stream during the forward leaves the rest to it: the
                             kernels size their grids to sm_budget SMs.  No counterpart in
                             the reference.  Added in version 1.1.0. */
+  int32_t group_kernel;  /* HYPERION_GROUP_*: the kernel of the grouped runs of the row path.
+                            No counterpart in the reference.  Added in version 1.2.0. */
 } hyperion_options;
 
 /* Bytes of device workspace the forward needs for these sizes with the automatic
@@ -177,12 +187,16 @@ int hyperion_read_device_errors(void* workspace, size_t workspace_bytes, void* s
  *   [0] SM count            [1] row kernel CTAs per SM   [2] row kernel shared bytes
  *   [3] tile kernel CTAs/SM [4] tile kernel shared bytes [5] row kernel CTAs per SM, head_dim 256
  *   [6] tile kernel loaded  [7] row kernel threads       [8] grouped row kernel threads
- *   [9] grouped row kernel CTAs per SM  [10] its shared bytes  [11] tile kernel threads */
+ *   [9] grouped row kernel CTAs per SM  [10] its shared bytes  [11] tile kernel threads
+ *   [12] tensor-core grouped kernel threads (0 when it did not load)
+ *   [13] its CTAs per SM    [14] its shared bytes */
 int hyperion_launch_info(int32_t* out, int32_t n);
 
 /* What the last forward on this thread did: out[0] = path (HYPERION_PATH_ROW or
  * _TILE, 0 when nothing was launched), out[1] = KV splits per item, out[2] = kernels
- * launched, out[3] = grid size of the main kernel.  Fills up to `n` values. */
+ * launched, out[3] = grid size of the main kernel, out[4] = the main kernel: 1 row
+ * kernel, 2 grouped kernel on the CUDA cores, 3 grouped kernel on the tensor core,
+ * 4 tile kernel (0 when nothing was launched).  Fills up to `n` values. */
 int hyperion_last_call_info(int32_t* out, int32_t n);
 
 /* Last CUDA error string seen by the library on this thread ("" if none). */

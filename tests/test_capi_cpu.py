@@ -31,7 +31,7 @@ def test_library_loads_and_exports_every_declared_symbol(hyperion):
     lib = ctypes.CDLL(hyperion.library_path())
     for name in _declared_functions():
         assert hasattr(lib, name), name
-    assert lib.hyperion_version() == 10100
+    assert lib.hyperion_version() == 10200
 
 
 def test_drop_in_names_match_reference_module(hyperion):
@@ -168,4 +168,4 @@ def test_launch_table_is_a_measured_grid():
         seen.add((kernel, items, keys))
         assert int(splits) in (1, 2, 3, 4, 6, 8, 12, 16)
         assert float(best_ms) <= float(rule_ms) * 1.01
-    assert {k for k, _, _ in seen} == {"0", "1"}
+    assert {k for k, _, _ in seen} == {"0", "1", "2"}

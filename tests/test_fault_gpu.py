@@ -21,38 +21,42 @@ DEV = torch.device("cuda", 0)
 SHORT = 2_000_000  # SM clock cycles, about a millisecond
 
 
-def _forward(hyperion, g, o, path, kv_group=1):
+def _forward(hyperion, g, o, path, kv_group=1, group_kernel="auto"):
     hyperion.hyperion_apex_kernel(g.worklist, g.total_work, g.q, None, g.k, None, g.v, g.v_scale, g.ctx_lens,
                                   g.block_tables, o, g.seq_q, g.head_dim, g.head_dim // 8, g.block_size,
-                                  g.num_blocks, g.inv_sqrt_d, g.causal, path=path, kv_group=kv_group)
+                                  g.num_blocks, g.inv_sqrt_d, g.causal, path=path, kv_group=kv_group,
+                                  group_kernel=group_kernel)
 
 
 def _cases():
     return [
-        ("tile", W.make_dense("f_tile", 1, 4, 512, 512, causal=True, o_dtype=torch.float32, seed=81), 1),
-        ("row", W.make_dense("f_row", 2, 4, 1, 2000, o_dtype=torch.float32, seed=82), 1),
-        ("row", W.make_dense("f_gqa", 2, 8, 1, 2000, kv_heads=2, o_dtype=torch.float32, seed=83), 4),
+        ("tile", W.make_dense("f_tile", 1, 4, 512, 512, causal=True, o_dtype=torch.float32, seed=81), 1, "auto"),
+        ("row", W.make_dense("f_row", 2, 4, 1, 2000, o_dtype=torch.float32, seed=82), 1, "auto"),
+        ("row", W.make_dense("f_gqa", 2, 8, 1, 2000, kv_heads=2, o_dtype=torch.float32, seed=83), 4, "cuda"),
+        # 128-key stages: 8000 keys in 8 pieces leave every CTA 8 stages, so the
+        # fourth exists to be left unarmed
+        ("row", W.make_dense("f_gqa_mma", 2, 8, 1, 8000, kv_heads=2, o_dtype=torch.float32, seed=84), 4, "mma"),
     ]
 
 
-@pytest.mark.parametrize("case", range(3), ids=["tile", "row", "grouped_row"])
+@pytest.mark.parametrize("case", range(4), ids=["tile", "row", "grouped_row", "grouped_mma"])
 @pytest.mark.parametrize("stage", [0, 3])
 def test_a_wait_that_runs_out_unwinds_and_the_next_call_is_correct(hyperion, oracle, case, stage):
-    path, wk, kv_group = _cases()[case]
+    path, wk, kv_group, group_kernel = _cases()[case]
     g = wk.to(DEV)
     ref, _, _, _ = oracle.forward_workload_c(wk)
     for rep in range(2):
         o = torch.full((g.n_bh * g.seq_q, g.head_dim), float("nan"), dtype=torch.float32, device=DEV)
         hyperion.read_device_errors(DEV, clear=True)
         hyperion.debug_fault(SHORT, stage)
-        _forward(hyperion, g, o, path, kv_group)
+        _forward(hyperion, g, o, path, kv_group, group_kernel)
         torch.cuda.synchronize()  # the call came back: the unwind ended every wait
         err = hyperion.read_device_errors(DEV, clear=True)
         assert err & hyperion.DEVERR_WAIT_TIMEOUT, (path, err)
         assert hyperion.last_call_info()["path"] == path
         # The same device, workspace and library: a normal call is correct.
         o2 = g.new_output()
-        _forward(hyperion, g, o2, path, kv_group)
+        _forward(hyperion, g, o2, path, kv_group, group_kernel)
         assert hyperion.read_device_errors(DEV, clear=True) == 0
         ok, mx, mn = oracle.tolerance_check(o2.cpu().numpy(), ref, 2e-2, 2e-3)
         assert ok, (path, rep, mx, mn)
@@ -61,7 +65,7 @@ def test_a_wait_that_runs_out_unwinds_and_the_next_call_is_correct(hyperion, ora
 def test_the_hook_is_consumed_by_one_call(hyperion, oracle):
     """A short bound with no unarmed stage changes nothing for a healthy call, and the
     hook does not outlive the call it was armed for."""
-    _, wk, _ = _cases()[0]
+    _, wk, _, _ = _cases()[0]
     g = wk.to(DEV)
     ref, _, _, _ = oracle.forward_workload_c(wk)
     hyperion.read_device_errors(DEV, clear=True)

@@ -83,3 +83,16 @@ def test_device_worklist_drives_the_forward(hyperion, oracle):
                                   grid=grid, block=block, shared=shared)
     assert hyperion.last_call_info()["path"] == "row"
     assert hyperion.last_call_info()["grid"] <= grid[0]
+    # Grouped-query decode (4 query heads per KV head): the tensor-core grouped
+    # kernel's 192-thread CTAs (producer, four query warps, MMA issuer).
+    grid, block, shared = glue.launch_config(dev, kv_group=4)
+    if info["group_mma_threads"]:
+        assert block == (info["group_mma_threads"], 1, 1) == (192, 1, 1)
+        assert grid[0] == info["sm_count"] * info["group_mma_ctas_per_sm"] and shared == info["group_mma_smem_bytes"]
+        gq = W.make_dense("lc_gqa", 2, 8, 1, 300, kv_heads=2, o_dtype=torch.float32, seed=6).to(dev)
+        og = gq.new_output()
+        hyperion.hyperion_apex_kernel(gq.worklist, gq.total_work, gq.q, None, gq.k, None, gq.v, gq.v_scale,
+                                      gq.ctx_lens, gq.block_tables, og, 1, 128, 16, gq.block_size, gq.num_blocks,
+                                      gq.inv_sqrt_d, False, kv_group=gq.kv_group, grid=grid, block=block, shared=shared)
+        assert hyperion.last_call_info()["kernel"] == "group_mma"
+        assert hyperion.last_call_info()["grid"] <= grid[0]

@@ -68,8 +68,9 @@ def test_gqa_paged_decode(hyperion, oracle, num_splits):
 def test_gqa_equals_block_tables_repeated_per_query_head(hyperion, oracle):
     """The same problem given to the ungrouped kernel, every query head's block-table
     row pointing at its KV head's pages.  Both meet the bar against the oracle, and
-    they agree with each other to rounding: both kernels sum the same 32-key groups of
-    f16x2 products, so any difference comes from a different split of the keys."""
+    they agree with each other to rounding: the grouped runs take their products on
+    the tensor core with f32 sums, the ungrouped kernel sums 32-key groups of f16x2
+    products, and the two split the keys differently."""
     wk = W.make_paged("gqa_eq", 3, 8, [100, 999, 3000], page=16, seed=53, o_dtype=torch.float32, kv_heads=2)
     o_g, err, _, _ = run(hyperion, wk, path="row", num_splits=2)
     assert err == 0

@@ -448,12 +448,12 @@ def test_forwards_on_two_streams_do_not_share_a_workspace(hyperion, oracle):
         check(oracle, wk, o.cpu().numpy())
 
 
-@pytest.mark.parametrize("kv_heads,splits", [(None, 8), (8, 16)])
-def test_split_choice_follows_the_measured_table(hyperion, oracle, kv_heads, splits):
+@pytest.mark.parametrize("kv_heads,group_kernel,splits", [(None, "auto", 8), (8, "cuda", 16), (8, "auto", 8)])
+def test_split_choice_follows_the_measured_table(hyperion, oracle, kv_heads, group_kernel, splits):
     """On a 148-SM B200 the automatic split count for a shape the launch table
     measured is the table's (128 query rows x 8192 keys: 8 pieces on the row kernel;
-    the same with 4 query heads per KV head: 16 pieces on the grouped kernel), and the
-    result is still the oracle's."""
+    the same with 4 query heads per KV head: 16 pieces on the CUDA-core grouped
+    kernel, 8 on the tensor-core one), and the result is still the oracle's."""
     if hyperion.launch_info()["sm_count"] != 148:
         pytest.skip("the launch table was measured on 148 SMs")
     wk = W.make_dense("t", 4, 32, 1, 8192, kv_heads=kv_heads, o_dtype=torch.float32, seed=66)
@@ -462,7 +462,7 @@ def test_split_choice_follows_the_measured_table(hyperion, oracle, kv_heads, spl
     o = g.new_output()
     hyperion.hyperion_apex_kernel(g.worklist, g.total_work, g.q, None, g.k, None, g.v, g.v_scale, g.ctx_lens,
                                   g.block_tables, o, 1, 128, 16, g.block_size, g.num_blocks, g.inv_sqrt_d, False,
-                                  kv_group=g.kv_group)
+                                  kv_group=g.kv_group, group_kernel=group_kernel)
     info = hyperion.last_call_info()
     assert info["splits"] == splits, info
     rows = list(range(0, g.n_bh, 7))
