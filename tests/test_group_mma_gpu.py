@@ -109,30 +109,43 @@ def test_a_nan_code_outside_every_context_does_not_matter(hyperion, oracle):
     check(oracle, wk, o)
 
 
-def _staged_keys(sign, inv_sqrt_d):
-    """4 query heads over one KV head, all four queries equal, 256 keys in four
-    64-key stages whose scores climb from -128 to 0 to +128 (the order reversed for a
-    negative inv_sqrt_d, so that the scaled scores always climb): the running max
-    moves twice, by more than 10 each time, and every query uses three epochs."""
-    wk = W.make_dense("mma_epochs", 1, 4, 1, 256, kv_heads=1, o_dtype=torch.float32, seed=207)
+def _staged_keys(levels, inv_sqrt_d):
+    """4 query heads over one KV head, all four queries equal, one 128-key stage per
+    entry of `levels`, every key of stage i scoring levels[i] (its sign bits differ
+    from the query's in (128 - level) / 2 places)."""
+    wk = W.make_dense("mma_epochs", 1, 4, 1, 128 * len(levels), kv_heads=1, o_dtype=torch.float32, seed=207)
     q = wk.q[0].clone()
     wk.q[:] = q
-    low = torch.bitwise_not(q)                      # score -128
-    mid = q ^ torch.tensor([-1, -1, 0, 0], dtype=torch.int32)  # 64 bits differ: score 0
-    order = [low, mid, q] if sign > 0 else [q, mid, low]
-    for st, rowv in enumerate(order):
-        wk.k[64 * st:64 * (st + 1)] = rowv
+    for st, level in enumerate(levels):
+        nd = (128 - level) // 2
+        bits = torch.zeros(128, dtype=torch.int64)
+        bits[:nd] = 1
+        flip = (bits.view(4, 32) << torch.arange(32)).sum(1)
+        flip = torch.where(flip >= 2**31, flip - 2**32, flip).to(torch.int32)
+        wk.k[128 * st:128 * (st + 1)] = q ^ flip
     wk.inv_sqrt_d = inv_sqrt_d
     return wk
 
 
 @pytest.mark.parametrize("inv_sqrt_d", [0.117, -0.1, 0.088])
 def test_running_max_moves_open_new_epochs(hyperion, oracle, inv_sqrt_d):
-    wk = _staged_keys(1 if inv_sqrt_d > 0 else -1, inv_sqrt_d)
+    """Scaled scores that climb stage by stage by more than ln 4 (the levels reversed
+    for a negative inv_sqrt_d): the running max moves at every stage and each query
+    uses all four epochs; one split or two."""
+    levels = [-128, -64, 0, 128] if inv_sqrt_d > 0 else [128, 64, 0, -128]
+    wk = _staged_keys(levels, inv_sqrt_d)
     for splits in (1, 2):
         o, err, _, info = run(hyperion, wk, num_splits=splits)
         assert err == 0 and info["kernel"] == "group_mma"
         check(oracle, wk, o)
+
+
+def test_a_fifth_move_redoes_the_run_exactly(hyperion, oracle):
+    """Five climbing stages need a fifth epoch: the run is redone on the CUDA cores."""
+    wk = _staged_keys([-128, -64, 0, 64, 128], 0.117)
+    o, err, _, info = run(hyperion, wk, num_splits=1)
+    assert err == 0 and info["kernel"] == "group_mma"
+    check(oracle, wk, o)
 
 
 def test_flat_weights(hyperion, oracle):
@@ -188,3 +201,27 @@ def test_bad_pages_and_items_are_flagged(hyperion, oracle):
     assert np.isnan(o[5]).all()
     rows = [r for r in range(wk.n_bh) if r != 5]
     check(oracle, wk, o, rows=rows)
+
+
+@pytest.mark.parametrize("page,kernel", [(8, "group_mma"), (32, "group_mma"), (64, "group_mma"), (128, "group_mma"),
+                                         (256, "group_mma"), (24, "group"), (4, "group")])
+def test_page_sizes(hyperion, oracle, page, kernel):
+    """A tensor-map box per page for pages of 8 to 128 keys dividing a 128-key stage,
+    one box per stage for pages of a multiple of 128 keys; other page sizes take the
+    CUDA-core grouped kernel.  Contexts end mid-page and mid-stage."""
+    wk = W.make_paged("mma_pages", 3, 8, [77, 1000, 2431], page=page, seed=215, o_dtype=torch.float32,
+                      kv_heads=2)
+    o, err, _, info = run(hyperion, wk, num_splits=3)
+    assert err == 0 and info["kernel"] == kernel, info
+    check(oracle, wk, o)
+
+
+@pytest.mark.parametrize("S_kv", [5, 100, 300])
+def test_short_contiguous_rows(hyperion, oracle, S_kv):
+    """The contiguous layout (one page per row): a row shorter than a stage is one
+    box of its own length; a longer one ends with a box that runs into the next row
+    (or past the pool, where the copy fills zeros), whose extra keys are zeroed."""
+    wk = W.make_dense("mma_short", 2, 8, 1, S_kv, kv_heads=2, o_dtype=torch.float32, seed=216)
+    o, err, _, info = run(hyperion, wk)
+    assert err == 0 and info["kernel"] == "group_mma", info
+    check(oracle, wk, o)
