@@ -271,10 +271,19 @@ __device__ __forceinline__ float pexp_mufu(uint32_t s, const PExp& x) {
   return ex2_approx(fmaf(__uint_as_float(s), x.k2, x.bias));
 }
 
+// Two weights from two scores with one packed f32x2 FMA (half the FMA-pipe
+// instructions of the softmax's exponent arguments) and two exponentials.
+__device__ __forceinline__ void pexp2(uint32_t s0, uint32_t s1, const PExp& x, float& e0, float& e1) {
+  const float2 t = __ffma2_rn(make_float2(__uint_as_float(s0), __uint_as_float(s1)), make_float2(x.k2, x.k2),
+                              make_float2(x.bias, x.bias));
+  e0 = ex2_approx(t.x);
+  e1 = ex2_approx(t.y);
+}
+
 // Weights of one 16-column chunk.
 __device__ __forceinline__ void p_exp16(const uint32_t (&v)[16], const PExp& x, float (&e)[16]) {
 #pragma unroll
-  for (int i = 0; i < 16; ++i) e[i] = pexp_mufu(v[i], x);
+  for (int i = 0; i < 16; i += 2) pexp2(v[i], v[i + 1], x, e[i], e[i + 1]);
 }
 
 // Finishes chunk h (exponentials in `e`: mask, add to l[], pack to f16 pairs, store
@@ -283,20 +292,17 @@ __device__ __forceinline__ void p_exp16(const uint32_t (&v)[16], const PExp& x, 
 // 8 cycles, and the finishing work of chunk h fills the issue slots in between.
 template <bool kMasked, bool kNext>
 __device__ __forceinline__ void p_step(uint32_t s_col, int h, float (&e)[16], uint32_t bits, const uint32_t (&vn)[16],
-                                       float (&en)[16], const PExp& x, float (&l)[4]) {
+                                       float (&en)[16], const PExp& x, float2& l) {
   uint32_t pk[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    if (kNext) {
-      en[2 * i] = pexp_mufu(vn[2 * i], x);
-      en[2 * i + 1] = pexp_mufu(vn[2 * i + 1], x);
-    }
+    if (kNext) pexp2(vn[2 * i], vn[2 * i + 1], x, en[2 * i], en[2 * i + 1]);
     float e0 = e[2 * i], e1 = e[2 * i + 1];
     if (kMasked) {
       e0 = ((bits >> (2 * i)) & 1u) ? e0 : 0.f;
       e1 = ((bits >> (2 * i + 1)) & 1u) ? e1 : 0.f;
     }
-    l[i & 3] += e0 + e1;
+    l = __fadd2_rn(l, make_float2(e0, e1));
     pk[i] = pack_f16x2(e0, e1);
   }
   tc::st8(s_col + 8 * h, pk);
@@ -309,7 +315,7 @@ __device__ __forceinline__ void p_step(uint32_t s_col, int h, float (&e)[16], ui
 template <bool kMasked>
 __device__ __forceinline__ float row_half_p(uint32_t s_col, const uint32_t (&mk)[4], int c0, int kbase, int row_end,
                                            const PExp& x) {
-  float l[4] = {0.f, 0.f, 0.f, 0.f};
+  float2 l = make_float2(0.f, 0.f);
   uint32_t va[16], vb[16];
   float ea[16], eb[16];
   tc::ld16(s_col, va);
@@ -325,7 +331,7 @@ __device__ __forceinline__ float row_half_p(uint32_t s_col, const uint32_t (&mk)
   tc::ld_wait_regs(vb);
   p_step<kMasked, true>(s_col, 2, ea, kMasked ? chunk_bits(mk, c0 + 2, kbase, row_end) : 0xFFFFu, vb, eb, x, l);
   p_step<kMasked, false>(s_col, 3, eb, kMasked ? chunk_bits(mk, c0 + 3, kbase, row_end) : 0xFFFFu, va, ea, x, l);
-  return (l[0] + l[1]) + (l[2] + l[3]);
+  return l.x + l.y;
 }
 
 // O row *= alpha (lanes that need no rescale pass alpha = 1).
