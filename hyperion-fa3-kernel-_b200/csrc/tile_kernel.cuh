@@ -119,17 +119,23 @@ __device__ __forceinline__ uint4 expand16(uint32_t b) {
   return o;
 }
 
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t r;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-  return r;
+// Four FP8 codes (dims d .. d+3) -> two f16x2 words, each value the reference's
+// decode / 256, in the order {d, d+2}, {d+1, d+3}: V tiles hold every group of 4
+// dims as d, d+2, d+1, d+3, so O's TMEM columns come out in that order too and the
+// epilogue swaps them back (register renaming, no instruction).
+__device__ __forceinline__ void fp8x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  lo = fp8x2_even_to_f16x2_div256(w);  // {b0, b2}
+  hi = fp8x2_odd_to_f16x2_div256(w);   // {b1, b3}
 }
 
-// Four FP8 codes -> two f16x2 words in dim order, each value the reference's decode / 256.
-__device__ __forceinline__ void fp8x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  const uint32_t s = prmt(w, 0u, 0x3120u);  // bytes b0 b2 b1 b3
-  lo = fp8x2_even_to_f16x2_div256(s);       // {b0, b1}
-  hi = fp8x2_odd_to_f16x2_div256(s);        // {b2, b3}
+// O columns of one 16-column chunk in dim order: columns hold dims d, d+2, d+1, d+3.
+__device__ __forceinline__ void dims_in_order(float (&f)[16]) {
+#pragma unroll
+  for (int g = 0; g < 16; g += 4) {
+    const float t = f[g + 1];
+    f[g + 1] = f[g + 2];
+    f[g + 2] = t;
+  }
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
@@ -196,6 +202,7 @@ __device__ __forceinline__ void store_o_row(void* o, long long o_base, uint32_t 
       float f[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) f[i] = __uint_as_float(v[i]) * scale;
+      dims_in_order(f);
       store_row16<kDtype>(o, o_base + 16 * c, f, sectors);
     }
   }
