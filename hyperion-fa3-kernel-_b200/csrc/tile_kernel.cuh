@@ -201,7 +201,12 @@ __device__ __forceinline__ void store_o_row(void* o, long long o_base, uint32_t 
     if (row_ok) {
       float f[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) f[i] = __uint_as_float(v[i]) * scale;
+      for (int i = 0; i < 16; i += 2) {
+        const float2 t = __fmul2_rn(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])),
+                                    make_float2(scale, scale));
+        f[i] = t.x;
+        f[i + 1] = t.y;
+      }
       dims_in_order(f);
       store_row16<kDtype>(o, o_base + 16 * c, f, sectors);
     }
