@@ -16,8 +16,11 @@ data-path collective).  The same line carries sub-records, measured in the same
 run with the same method, for the decode workloads (whose metric is HBM GB/s)
 and the long-context prefill (B1 H64 S32768, heads split over the ranks:
 strong scaling).  At N > 1 every record also carries `with_gather`: the same
-steps with the all-gather of O (NCCL) inside each step, serial and overlapped
-with the forward (the faster one is its value).
+steps with the whole O gathered on every rank inside each step, in three forms:
+the forward then an NCCL all-gather (serial), the forward in chunks whose
+all-gathers overlap the next chunk (overlapped), and the forward storing its O
+rows into every rank's output buffer over NVLink itself (fused); the fastest one
+is its value.
 
 Timing: W untimed warm-up steps; L2 flushed (256 MiB write) before every timed
 step unless the inputs are larger than twice the L2; each step bracketed by CUDA
@@ -581,7 +584,7 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
     # whose gathers (on a second stream) overlap the next run's compute, with the
     # forward's persistent grid kept off GATHER_SMS SMs so that NCCL's kernels find
     # room beside it.
-    gather_total = serial_total = 0.0
+    gather_total = serial_total = fused_total = 0.0
     if world > 1:
         from hyperion_b200 import sharding as S
 
@@ -606,8 +609,18 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
         def overlapped_step():
             S.forward_and_gather(forward_chunk, chunks, o, out_chunks, comm_stream=comm)
 
+        # fused: the forward stores its O rows into this rank's slot of every rank's
+        # gathered buffer (peer stores over NVLink, CUDA IPC mappings), then a 4-byte
+        # all-reduce stands as the barrier after which every rank may read its copy.
+        peer = S.PeerOutput(o.shape[0], o.shape[1], o.dtype, dev)
+        tick = torch.zeros(1, dtype=torch.int32, device=dev)
+
+        def fused_step():
+            call_forward(hyperion, wk, peer.local, path=args.path, o_peers=peer.o_peers)
+            pg.all_reduce(tick)
+
         totals = []
-        for step in (serial_step, overlapped_step):
+        for step in (serial_step, overlapped_step, fused_step):
             step()
             torch.cuda.synchronize()
             g_st = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -623,25 +636,31 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
             torch.cuda.synchronize()
             barrier()
             totals.append(sum(s.elapsed_time(e) for s, e in zip(g_st, g_en)))
-        serial_total, gather_total = totals
+        serial_total, gather_total, fused_total = totals
         # The overlapped output is the serial one, rank by rank (a chunked call may
-        # choose other KV splits, so the two agree to rounding, not bit for bit).
+        # choose other KV splits, so the two agree to rounding, not bit for bit); the
+        # fused output is the serial one bit for bit (the same call, stored twice).
         diff = (out_chunks.transpose(0, 1).reshape(out_all.shape).float() - out_all.float()).abs().max().item()
         if not diff <= 2e-2:
             raise RuntimeError(f"overlapped gather differs from the serial gather by {diff}")
-        del out_all, out_chunks
+        fused_same = torch.equal(peer.out.view(torch.uint8), out_all.view(torch.uint8))
+        peer.close()
+        if not fused_same:
+            raise RuntimeError("the fused gather differs from the serial gather")
+        del out_all, out_chunks, peer
 
-    vals = torch.tensor([total_ms, e2e_ms, float(pairs), gather_total, serial_total], dtype=torch.float64,
-                        device=dev)
+    vals = torch.tensor([total_ms, e2e_ms, float(pairs), gather_total, serial_total, fused_total],
+                        dtype=torch.float64, device=dev)
     if pg is not None:
         mx = vals.clone()
         pg.all_reduce(mx, op=pg.ReduceOp.MAX)
         sm = vals.clone()
         pg.all_reduce(sm, op=pg.ReduceOp.SUM)
         total_ms_max, e2e_ms_max, gather_max, serial_max = float(mx[0]), float(mx[1]), float(mx[3]), float(mx[4])
+        fused_max = float(mx[5])
         pairs_all = float(sm[2])
     else:
-        total_ms_max, e2e_ms_max, gather_max, serial_max = total_ms, e2e_ms, 0.0, 0.0
+        total_ms_max, e2e_ms_max, gather_max, serial_max, fused_max = total_ms, e2e_ms, 0.0, 0.0, 0.0
         pairs_all = float(pairs)
 
     rec = None
@@ -684,16 +703,21 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
             rec["hbm_gbs"] = roof["achieved"]
         if world > 1:
             o_bytes = o.numel() * o.element_size()
-            best = min(gather_max, serial_max)
+            forms = {"fused": fused_max, "overlapped": gather_max, "serial": serial_max}
+            form = min(forms, key=forms.get)
+            best = forms[form]
             rec["with_gather"] = {
                 "value": pairs_all * args.steps / (best * 1e-3), "unit": "pairs/s",
                 "ms_per_step": best / args.steps,
-                "form": "overlapped" if gather_max <= serial_max else "serial",
+                "form": form,
+                "fused_ms_per_step": fused_max / args.steps,
                 "overlapped_ms_per_step": gather_max / args.steps,
                 "serial_ms_per_step": serial_max / args.steps,
                 "gather_bytes_received_per_rank": o_bytes * (world - 1),
                 "nvlink_floor_ms": o_bytes * (world - 1) / NVLINK_GBS / 1e6,
-                "mode": (f"the faster of two forms, max over ranks: overlapped = the forward in {GATHER_CHUNKS} runs of "
+                "mode": ("the fastest of three forms, max over ranks: fused = the forward storing each O row into "
+                         "every rank's gathered buffer as well (peer stores over NVLink into CUDA IPC mappings), then "
+                         f"a 4-byte NCCL all-reduce as the barrier; overlapped = the forward in {GATHER_CHUNKS} runs of "
                          f"(batch, head) rows on {GATHER_SMS} fewer SMs, each run's O all-gathered (NCCL "
                          "all_gather_into_tensor, second stream) while the next computes; serial = the forward, then "
                          "one all-gather"),

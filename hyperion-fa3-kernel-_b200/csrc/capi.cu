@@ -231,7 +231,7 @@ size_t workspace_needed(const DevInfo& di, int total_work, int D, int block_size
 
 extern "C" {
 
-int32_t hyperion_version(void) { return 1 * 10000 + 2 * 100 + 0; }
+int32_t hyperion_version(void) { return 1 * 10000 + 3 * 100 + 0; }
 
 const char* hyperion_last_error_string(void) { return g_last_error.c_str(); }
 
@@ -352,6 +352,21 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   // pool when the pool holds n_bh * num_blocks pages.
   p.pages_all_valid = (!paged && (long long)ext->n_bh * num_blocks <= p.pool_blocks) ? 1 : 0;
   p.o_align32 = (reinterpret_cast<uintptr_t>(O) % 32 == 0) ? 1 : 0;
+  // Peer copies of O: the same elements at the same indices, for a head-sharded
+  // caller whose ranks all hold the gathered output.
+  const int n_peers = opt ? opt->n_o_peers : 0;
+  if (n_peers < 0 || n_peers > hyp::kMaxOutPeers)
+    return fail(HYPERION_ERR_INVALID_ARG, "n_o_peers must be in [0, 7]");
+  if (n_peers > 0 && opt->o_peers == nullptr) return fail(HYPERION_ERR_INVALID_ARG, "o_peers is NULL");
+  p.n_o_peers = n_peers;
+  for (int k = 0; k < n_peers; ++k) {
+    void* q = opt->o_peers[k];
+    if (q == nullptr) return fail(HYPERION_ERR_INVALID_ARG, "an o_peers entry is NULL");
+    if (reinterpret_cast<uintptr_t>(q) % 16 != 0)
+      return fail(HYPERION_ERR_INVALID_ARG, "o_peers entries must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(q) % 32 != 0) p.o_align32 = 0;
+    p.o_peers[k] = q;
+  }
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.counters = reinterpret_cast<uint32_t*>(ws + hyp::kWsCounters);
   p.err = reinterpret_cast<uint32_t*>(ws + hyp::kWsError);
@@ -622,6 +637,49 @@ int noalloc_scratch(uint8_t** out) {
 }
 
 }  // namespace
+
+extern "C" {
+
+int hyperion_ipc_alloc(size_t bytes, void** ptr, uint8_t* handle) {
+  if (ptr == nullptr || handle == nullptr) return fail(HYPERION_ERR_INVALID_ARG, "ptr or handle is NULL");
+  if (bytes == 0) return fail(HYPERION_ERR_INVALID_ARG, "bytes is 0");
+  void* d = nullptr;
+  cudaError_t e = cudaMalloc(&d, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, d);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return cuda_fail(e, "cudaIpcGetMemHandle");
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == HYPERION_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  *ptr = d;
+  return HYPERION_OK;
+}
+
+int hyperion_ipc_open(const uint8_t* handle, void** ptr) {
+  if (ptr == nullptr || handle == nullptr) return fail(HYPERION_ERR_INVALID_ARG, "ptr or handle is NULL");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* d = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&d, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  *ptr = d;
+  return HYPERION_OK;
+}
+
+int hyperion_ipc_close(void* ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? HYPERION_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int hyperion_ipc_free(void* ptr) {
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? HYPERION_OK : cuda_fail(e, "cudaFree");
+}
+
+}  // extern "C"
 
 extern "C" int hyperion_apex_kernel_noalloc(const int32_t* worklist, int32_t total_work, const uint32_t* Q,
                                             const float* Q_scale, const uint32_t* K_cache, const float* K_scale,

@@ -29,6 +29,10 @@ constexpr size_t kWsCounters = 0;     // uint32[16]: [0] row-kernel ticket, [1] 
 constexpr size_t kWsError = 64;       // uint32 error flags
 constexpr size_t kWsPartials = 256;   // float partials of the split-KV row kernel
 
+// Copies of the output a forward may write besides O: the gathered output buffers of
+// the other ranks of a head-sharded forward, mapped into this process.
+constexpr int kMaxOutPeers = 7;
+
 struct FwdParams {
   const int4* worklist;
   int total_work;
@@ -60,6 +64,8 @@ struct FwdParams {
   int o_align32;        // 1: O is 32-byte aligned, so a 16-value row piece is whole 32-byte sectors
   long long wait_cycles;  // bound of every device wait: kWaitCycles, shorter only under a test hook
   int fault_stage;        // test hook: index of the KV stage the loading warp leaves unarmed (-1: none)
+  int n_o_peers;          // copies of O written beside it (0: none)
+  void* o_peers[kMaxOutPeers];  // each receives every output element at O's own index
 };
 
 // KV-side (batch, head) row of query row `bh`: grouped-query attention maps
@@ -326,6 +332,18 @@ __device__ __forceinline__ void store_out(void* o, int dtype, long long idx, flo
   } else {
     static_cast<__half*>(o)[idx] = __float2half_rn(x);
   }
+}
+
+// Final store of output element idx: to O and to every peer copy, same index.
+__device__ __forceinline__ void store_out_all(const FwdParams& p, long long idx, float x) {
+  store_out(p.o, p.o_dtype, idx, x);
+  for (int k = 0; k < p.n_o_peers; ++k) store_out(p.o_peers[k], p.o_dtype, idx, x);
+}
+
+// A CTA that wrote into peer copies makes its stores visible system-wide before it
+// exits; the caller's synchronisation after the forward then orders the readers.
+__device__ __forceinline__ void fence_out_peers(const FwdParams& p) {
+  if (p.n_o_peers > 0) __threadfence_system();
 }
 
 // Resolved key range of one work item: keys [0, kv_end) after the context length,

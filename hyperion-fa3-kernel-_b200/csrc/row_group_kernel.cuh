@@ -572,7 +572,7 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
               if (stop) continue;
               if (p.n_split == 1) {
                 const float inv_l = (L > 1e-6f) ? 1.f / L : 1.f;
-                store_out(p.o, p.o_dtype, (long long)sl.orow[j] * D + d, a * inv_l);
+                store_out_all(p, (long long)sl.orow[j] * D + d, a * inv_l);
               } else {
                 float* part = p.partials + ((long long)sl.item[j] * p.n_split + sl.split) * (2 + D);
                 part[2 + d] = a;
@@ -591,6 +591,7 @@ __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(F
       if (stop) break;
     }
   }
+  fence_out_peers(p);
 }
 
 }  // namespace row

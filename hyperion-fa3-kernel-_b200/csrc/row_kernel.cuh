@@ -427,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
         if (p.n_split == 1) {
           if (sl.valid) {
             const float inv_l = (L > 1e-6f) ? 1.f / L : 1.f;
-            store_out(p.o, p.o_dtype, (long long)sl.orow * D + d, a * inv_l);
+            store_out_all(p, (long long)sl.orow * D + d, a * inv_l);
           }
         } else {
           float* part = p.partials + (long long)sl.unit * (2 + D);
@@ -442,6 +442,7 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
       if (stop) break;
     }
   }
+  fence_out_peers(p);
 }
 
 // Merges the n_split partials (m, l, acc[D]) of every item and writes O.
@@ -463,8 +464,9 @@ __global__ void __launch_bounds__(128) row_combine_kernel(FwdParams p) {
       a += part[2 + d] * f;
     }
     const float inv_l = (L > 1e-6f) ? 1.f / L : 1.f;
-    store_out(p.o, p.o_dtype, ((long long)inf.bh * p.seq_q + inf.q_idx) * D + d, a * inv_l);
+    store_out_all(p, ((long long)inf.bh * p.seq_q + inf.q_idx) * D + d, a * inv_l);
   }
+  fence_out_peers(p);
 }
 
 }  // namespace row

@@ -229,7 +229,7 @@ __device__ __noinline__ void redo_query(const FwdParams& p, const row::RunSlot<k
     const float inv_l = (l > 1e-6f) ? 1.f / l : 1.f;
 #pragma unroll
     for (int i = 0; i < 4; ++i)
-      store_out(p.o, p.o_dtype, (long long)sl.orow[j] * kD + 4 * lane + i, acc[i] * vs * inv_l);
+      store_out_all(p, (long long)sl.orow[j] * kD + 4 * lane + i, acc[i] * vs * inv_l);
   } else {
     float* part = p.partials + ((long long)sl.item[j] * p.n_split + sl.split) * (2 + kD);
 #pragma unroll
@@ -612,7 +612,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
               const float L = sm.run_l[rp][j];
               if (p.n_split == 1) {
                 const float inv_l = (L > 1e-6f) ? 1.f / L : 1.f;
-                store_out(p.o, p.o_dtype, (long long)sl.orow[j] * kD + d, o[j] * vs * inv_l);
+                store_out_all(p, (long long)sl.orow[j] * kD + d, o[j] * vs * inv_l);
               } else {
                 // x = 64 w: both sums back to weight units, exactly.
                 float* part = p.partials + ((long long)sl.item[j] * p.n_split + sl.split) * (2 + kD);
@@ -634,6 +634,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     }
   }
 
+  fence_out_peers(p);
   tc::fence_before_sync();
   __syncthreads();
   if (warp == kMmaWarp) {

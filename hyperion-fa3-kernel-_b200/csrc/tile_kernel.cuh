@@ -189,10 +189,11 @@ __device__ __forceinline__ void store_row16(void* o, long long base, const float
   }
 }
 
-// Epilogue of one row: O = acc * scale from TMEM to global memory, 16 columns at a time.
+// Epilogue of one row: O = acc * scale from TMEM to global memory (and to every peer
+// copy of O, same index), 16 columns at a time.
 template <int kDtype>
-__device__ __forceinline__ void store_o_row(void* o, long long o_base, uint32_t o_col, float scale, bool row_ok,
-                                            bool sectors) {
+__device__ __forceinline__ void store_o_row(const FwdParams& p, long long o_base, uint32_t o_col, float scale,
+                                            bool row_ok) {
 #pragma unroll 1
   for (int c = 0; c < 8; ++c) {
     uint32_t v[16];
@@ -208,23 +209,28 @@ __device__ __forceinline__ void store_o_row(void* o, long long o_base, uint32_t 
         f[i + 1] = t.y;
       }
       dims_in_order(f);
-      store_row16<kDtype>(o, o_base + 16 * c, f, sectors);
+      store_row16<kDtype>(p.o, o_base + 16 * c, f, p.o_align32);
+      for (int k = 0; k < p.n_o_peers; ++k) store_row16<kDtype>(p.o_peers[k], o_base + 16 * c, f, p.o_align32);
     }
   }
 }
 
-__device__ __forceinline__ void store_zero_row(void* o, int dtype, long long o_base, bool sectors) {
+__device__ __forceinline__ void store_zero_row(const FwdParams& p, long long o_base) {
   float z[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) z[i] = 0.f;
 #pragma unroll 1
-  for (int c = 0; c < 8; ++c) {
-    if (dtype == HYPERION_DTYPE_F32) {
-      store_row16<HYPERION_DTYPE_F32>(o, o_base + 16 * c, z, sectors);
-    } else if (dtype == HYPERION_DTYPE_BF16) {
-      store_row16<HYPERION_DTYPE_BF16>(o, o_base + 16 * c, z, sectors);
-    } else {
-      store_row16<HYPERION_DTYPE_F16>(o, o_base + 16 * c, z, sectors);
+  for (int k = -1; k < p.n_o_peers; ++k) {
+    void* o = k < 0 ? p.o : p.o_peers[k];
+#pragma unroll 1
+    for (int c = 0; c < 8; ++c) {
+      if (p.o_dtype == HYPERION_DTYPE_F32) {
+        store_row16<HYPERION_DTYPE_F32>(o, o_base + 16 * c, z, p.o_align32);
+      } else if (p.o_dtype == HYPERION_DTYPE_BF16) {
+        store_row16<HYPERION_DTYPE_BF16>(o, o_base + 16 * c, z, p.o_align32);
+      } else {
+        store_row16<HYPERION_DTYPE_F16>(o, o_base + 16 * c, z, p.o_align32);
+      }
     }
   }
 }
@@ -853,7 +859,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       const long long o_base = row_ok ? ((long long)u.bh * p.seq_q + q_idx) * 128 : 0;
       const int row_end = row_ok ? (p.causal ? min(u.ctx, q_idx + 1) : u.ctx) : 0;
       if (n_tiles == 0) {
-        if (row_ok) store_zero_row(p.o, p.o_dtype, o_base, p.o_align32);
+        if (row_ok) store_zero_row(p, o_base);
         have = fetch();
         continue;
       }
@@ -949,11 +955,11 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       const float vs = u.vs;
       const float scale = 256.f * vs * ((l > 1e-6f) ? 1.f / l : 1.f);
       if (p.o_dtype == HYPERION_DTYPE_BF16) {
-        store_o_row<HYPERION_DTYPE_BF16>(p.o, o_base, o_col, scale, row_ok, p.o_align32);
+        store_o_row<HYPERION_DTYPE_BF16>(p, o_base, o_col, scale, row_ok);
       } else if (p.o_dtype == HYPERION_DTYPE_F32) {
-        store_o_row<HYPERION_DTYPE_F32>(p.o, o_base, o_col, scale, row_ok, p.o_align32);
+        store_o_row<HYPERION_DTYPE_F32>(p, o_base, o_col, scale, row_ok);
       } else {
-        store_o_row<HYPERION_DTYPE_F16>(p.o, o_base, o_col, scale, row_ok, p.o_align32);
+        store_o_row<HYPERION_DTYPE_F16>(p, o_base, o_col, scale, row_ok);
       }
       tc::fence_before_sync();
       __syncwarp();
@@ -961,6 +967,7 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     }
   }
 
+  fence_out_peers(p);
   tc::fence_before_sync();
   __syncthreads();
   if (warp == kMmaWarp) {

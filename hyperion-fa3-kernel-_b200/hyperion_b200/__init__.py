@@ -52,7 +52,7 @@ from ._capi import (  # noqa: F401
 )
 
 HYPERION_LOADED = True
-__version__ = "1.2.0"
+__version__ = "1.3.0"
 
 _O_DTYPES = {torch.float16: _capi.DTYPE_F16, torch.bfloat16: _capi.DTYPE_BF16, torch.float32: _capi.DTYPE_F32}
 _PATHS = {"auto": _capi.PATH_AUTO, "row": _capi.PATH_ROW, "tile": _capi.PATH_TILE}
@@ -128,6 +128,7 @@ def hyperion_apex_kernel(
     kv_group: int = 1,
     sm_budget: int = 0,
     group_kernel: str = "auto",
+    o_peers=None,
 ) -> None:
     """Enqueues the forward on the current CUDA stream of O's device (asynchronous).
 
@@ -148,6 +149,12 @@ def hyperion_apex_kernel(
     `group_kernel` ("auto", "cuda" or "mma"): the kernel of the row path's grouped
     runs (kv_group > 1 or seq_q > 1): the P.V products on the tensor core where it
     applies (head_dim 128, a per-tensor or per-head V scale), else on the CUDA cores.
+
+    `o_peers` (up to 7 device addresses, ints): every output element is also written
+    there, at O's own index -- the other ranks' gathered outputs for a head-sharded
+    forward (`sharding.PeerOutput`), so that the forward also does the all-gather of
+    O by peer stores while it computes.  The caller synchronises the ranks before
+    any of them reads its gathered output.
     """
     total_work = int(total_work)
     _check(int(kv_group) >= 1, "kv_group must be >= 1")
@@ -200,10 +207,14 @@ def hyperion_apex_kernel(
 
     ext = _capi.Extents(n_kv, pool_rows, V_scale.numel(), bt_numel, _O_DTYPES[O.dtype],
                         _hint(grid), _hint(block), _hint(shared))
+    peers = list(o_peers or [])
+    _check(len(peers) <= _capi.MAX_OUT_PEERS, f"at most {_capi.MAX_OUT_PEERS} o_peers")
+    peer_arr = (ctypes.c_void_p * max(len(peers), 1))(*[int(x) for x in peers])
     opt = _capi.Options(_PATHS[path], int(num_splits),
                         debug_scores.data_ptr() if debug_scores is not None else None,
                         debug_scores.size(1) if debug_scores is not None else 0, int(kv_group), int(sm_budget),
-                        _GROUP_KERNELS[group_kernel])
+                        _GROUP_KERNELS[group_kernel],
+                        ctypes.cast(peer_arr, ctypes.POINTER(ctypes.c_void_p)) if peers else None, len(peers))
     with torch.cuda.device(dev):
         need = _capi.lib.hyperion_workspace_bytes(total_work, head_dim, block_size, num_blocks)
         _check(need > 0, f"hyperion_workspace_bytes failed: {_capi.last_error()}")
@@ -335,3 +346,36 @@ def last_call_info() -> dict:
 
 def library_path() -> str:
     return _capi.LIB_PATH
+
+
+def ipc_alloc(nbytes: int):
+    """Device memory other processes may map: (address, 64-byte IPC handle)."""
+    ptr = ctypes.c_void_p()
+    handle = (ctypes.c_uint8 * _capi.IPC_HANDLE_BYTES)()
+    rc = _capi.lib.hyperion_ipc_alloc(int(nbytes), ctypes.byref(ptr), handle)
+    if rc != _capi.HYPERION_OK:
+        raise RuntimeError(f"hyperion_ipc_alloc failed (status {rc}): {_capi.last_error()}")
+    return int(ptr.value), bytes(handle)
+
+
+def ipc_open(handle: bytes) -> int:
+    """Maps another process's ipc_alloc memory into this one; returns its address here."""
+    _check(len(handle) == _capi.IPC_HANDLE_BYTES, "an IPC handle is 64 bytes")
+    ptr = ctypes.c_void_p()
+    buf = (ctypes.c_uint8 * _capi.IPC_HANDLE_BYTES)(*handle)
+    rc = _capi.lib.hyperion_ipc_open(buf, ctypes.byref(ptr))
+    if rc != _capi.HYPERION_OK:
+        raise RuntimeError(f"hyperion_ipc_open failed (status {rc}): {_capi.last_error()}")
+    return int(ptr.value)
+
+
+def ipc_close(ptr: int) -> None:
+    rc = _capi.lib.hyperion_ipc_close(ctypes.c_void_p(ptr))
+    if rc != _capi.HYPERION_OK:
+        raise RuntimeError(f"hyperion_ipc_close failed (status {rc}): {_capi.last_error()}")
+
+
+def ipc_free(ptr: int) -> None:
+    rc = _capi.lib.hyperion_ipc_free(ctypes.c_void_p(ptr))
+    if rc != _capi.HYPERION_OK:
+        raise RuntimeError(f"hyperion_ipc_free failed (status {rc}): {_capi.last_error()}")

@@ -47,7 +47,14 @@ EXPORTED = (
     "hyperion_apex_kernel_noalloc",
     "hyperion_kv_cache_write",
     "hyperion_debug_fault",
+    "hyperion_ipc_alloc",
+    "hyperion_ipc_open",
+    "hyperion_ipc_close",
+    "hyperion_ipc_free",
 )
+
+IPC_HANDLE_BYTES = 64  # HYPERION_IPC_HANDLE_BYTES
+MAX_OUT_PEERS = 7
 
 # Fixed per-device scratch of hyperion_apex_kernel_noalloc (HYPERION_NOALLOC_SCRATCH_BYTES).
 NOALLOC_SCRATCH_BYTES = 32 << 20
@@ -75,6 +82,8 @@ class Options(ctypes.Structure):
         ("kv_group", ctypes.c_int32),
         ("sm_budget", ctypes.c_int32),
         ("group_kernel", ctypes.c_int32),
+        ("o_peers", ctypes.POINTER(ctypes.c_void_p)),
+        ("n_o_peers", ctypes.c_int32),
     ]
 
 
@@ -126,6 +135,15 @@ def _load() -> ctypes.CDLL:
                                             _vp, _vp, _i64, _vp, ctypes.c_size_t, _vp]
     lib.hyperion_debug_fault.restype = ctypes.c_int
     lib.hyperion_debug_fault.argtypes = [_i64, _i32]
+    _u8p = ctypes.POINTER(ctypes.c_uint8)
+    lib.hyperion_ipc_alloc.restype = ctypes.c_int
+    lib.hyperion_ipc_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(_vp), _u8p]
+    lib.hyperion_ipc_open.restype = ctypes.c_int
+    lib.hyperion_ipc_open.argtypes = [_u8p, ctypes.POINTER(_vp)]
+    lib.hyperion_ipc_close.restype = ctypes.c_int
+    lib.hyperion_ipc_close.argtypes = [_vp]
+    lib.hyperion_ipc_free.restype = ctypes.c_int
+    lib.hyperion_ipc_free.argtypes = [_vp]
     return lib
 
 

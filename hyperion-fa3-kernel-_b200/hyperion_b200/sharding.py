@@ -163,3 +163,84 @@ def gather_output(o_local: torch.Tensor, batch: int, n_heads: int, seq_q: int, g
     dist.all_gather(bufs, buf, group=group)
     parts = [bufs[r][: batch * len(head_range(n_heads, world, r, kv_group)) * seq_q] for r in range(world)]
     return assemble_heads(parts, batch, n_heads, seq_q, world, kv_group)
+
+
+class _DeviceArray:
+    """A plain device address, shape and numpy type string in the CUDA array
+    interface, so that torch.as_tensor wraps memory this package allocated."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+_TYPESTR = {torch.float32: ("<f4", torch.float32), torch.float16: ("<f2", torch.float16),
+            torch.bfloat16: ("<i2", torch.bfloat16)}
+
+
+class PeerOutput:
+    """The gathered output [world, rows, D] held in IPC memory on every rank, with
+    the other ranks' copies mapped into this process.
+
+    The forward writes its O rows into `local` (this rank's slot, out[rank]) and,
+    through `o_peers` (hyperion_apex_kernel's o_peers argument), the same rows into
+    slot `rank` of every other rank's copy over NVLink: when the forward on every
+    rank has finished, each rank holds the whole output and no gather collective
+    has run.  Stores only: no peer memory is read, and nothing is loaded through a
+    tensor map from it.
+
+    A step is forward(o=local, o_peers=o_peers) then a collective barrier (any
+    collective the ranks run after the forward on the same stream): a rank reads
+    `out` only after it, and a rank must not start the next forward until every
+    rank is done reading the last output (a second barrier, or the next step's
+    collective).  rows is the largest block of any rank (shards of unequal size are
+    padded to it); every rank of `group` constructs this with the same rows, D and
+    dtype, in the same order of collectives.  close() unmaps the peers and frees
+    the buffer after a barrier."""
+
+    def __init__(self, rows: int, d: int, dtype: torch.dtype, device, group=None):
+        import torch.distributed as dist
+
+        from . import ipc_alloc, ipc_open
+
+        if dtype not in _TYPESTR:
+            raise ValueError(f"unsupported output dtype {dtype}")
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world - 1 > 7:
+            raise ValueError(f"a world of {self.world} needs more than 7 output peers")
+        typestr, view = _TYPESTR[dtype]
+        esize = torch.tensor([], dtype=dtype).element_size()
+        slot = rows * d * esize
+        with torch.cuda.device(device):
+            self.ptr, handle = ipc_alloc(self.world * slot)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self._opened = []
+        with torch.cuda.device(device):
+            for r in range(self.world):
+                if r != self.rank:
+                    self._opened.append(ipc_open(handles[r]))
+        self.o_peers = [base + self.rank * slot for base in self._opened]
+        raw = torch.as_tensor(_DeviceArray(self.ptr, (self.world, rows, d), typestr), device=device)
+        self.out = raw.view(view)
+        self.local = self.out[self.rank]
+
+    def close(self) -> None:
+        import torch.distributed as dist
+
+        from . import ipc_close, ipc_free
+
+        if self.ptr is None:
+            return
+        torch.cuda.synchronize(self.out.device)
+        dist.barrier(group=self.group)
+        for base in self._opened:
+            ipc_close(base)
+        self._opened = []
+        self.o_peers = []
+        dist.barrier(group=self.group)
+        self.out = self.local = None
+        ipc_free(self.ptr)
+        self.ptr = None

@@ -122,6 +122,14 @@ typedef struct hyperion_options {
                             the reference.  Added in version 1.1.0. */
   int32_t group_kernel;  /* HYPERION_GROUP_*: the kernel of the grouped runs of the row path.
                             No counterpart in the reference.  Added in version 1.2.0. */
+  void* const* o_peers;  /* n_o_peers device pointers (at most 7), each written with every output
+                            element at O's own index, beside O.  A head-sharded caller passes the
+                            other ranks' gathered outputs, offset to this rank's rows and mapped
+                            into this process (hyperion_ipc_open): the forward then is also the
+                            all-gather of O, by peer stores over NVLink while it computes.  The
+                            caller synchronises the ranks before reading.  NULL / 0: none.
+                            No counterpart in the reference.  Added in version 1.3.0. */
+  int32_t n_o_peers;
 } hyperion_options;
 
 /* Bytes of device workspace the forward needs for these sizes with the automatic
@@ -198,6 +206,17 @@ int hyperion_launch_info(int32_t* out, int32_t n);
  * kernel, 2 grouped kernel on the CUDA cores, 3 grouped kernel on the tensor core,
  * 4 tile kernel (0 when nothing was launched).  Fills up to `n` values. */
 int hyperion_last_call_info(int32_t* out, int32_t n);
+
+/* Device memory that other processes may map: `bytes` from cudaMalloc (CUDA IPC needs an
+ * allocation's base), and its HYPERION_IPC_HANDLE_BYTES-byte handle for them.  With
+ * hyperion_ipc_open another process maps it (peer access enabled as needed); release with
+ * hyperion_ipc_close there and hyperion_ipc_free here.  The gathered output of a head-sharded
+ * forward (hyperion_options.o_peers) lives in such buffers.  No counterpart in the reference. */
+#define HYPERION_IPC_HANDLE_BYTES 64
+int hyperion_ipc_alloc(size_t bytes, void** ptr, uint8_t* handle);
+int hyperion_ipc_open(const uint8_t* handle, void** ptr);
+int hyperion_ipc_close(void* ptr);
+int hyperion_ipc_free(void* ptr);
 
 /* Last CUDA error string seen by the library on this thread ("" if none). */
 const char* hyperion_last_error_string(void);

@@ -1,0 +1,162 @@
+"""The output written to peer buffers as well as O (hyperion_apex_kernel o_peers).
+
+On one GPU the "peers" are other buffers of the same device: every kernel (tile,
+row with and without KV splits, both grouped kernels) must leave each of them equal
+to O, bit for bit, and O itself must still meet the oracle bar.  On two GPUs,
+PeerOutput maps each rank's gathered buffer into the other rank and the forward
+stores its head block into both; the result must equal the NCCL all-gather of the
+same blocks, bit for bit.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from hyperion_b200 import sharding as S
+from hyperion_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+MEAN_ABS = 2e-3
+
+
+def _workload(kind, o_dtype):
+    if kind == "prefill":
+        return W.make_dense("po_pre", 2, 3, 300, 300, causal=True, o_dtype=o_dtype, seed=81)
+    if kind == "decode":
+        return W.make_dense("po_dec", 3, 4, 1, 5000, o_dtype=o_dtype, seed=82)
+    if kind == "paged":
+        return W.make_paged("po_paged", 4, 4, [17, 300, 1000, 2500], page=16, seed=83, o_dtype=o_dtype)
+    if kind == "gqa":
+        return W.make_dense("po_gqa", 3, 8, 1, 3000, o_dtype=o_dtype, seed=84, kv_heads=2)
+    raise ValueError(kind)
+
+
+CASES = [
+    ("prefill", "tile", "auto", 0, torch.bfloat16),
+    ("prefill", "tile", "auto", 0, torch.float16),
+    ("prefill", "tile", "auto", 0, torch.float32),
+    ("prefill", "row", "auto", 0, torch.bfloat16),
+    ("decode", "row", "auto", 1, torch.bfloat16),
+    ("decode", "row", "auto", 3, torch.float32),
+    ("paged", "auto", "auto", 0, torch.bfloat16),
+    ("gqa", "row", "cuda", 0, torch.bfloat16),
+    ("gqa", "row", "mma", 0, torch.float32),
+    ("gqa", "row", "mma", 2, torch.bfloat16),
+]
+
+
+@pytest.mark.parametrize("kind,path,group_kernel,num_splits,o_dtype", CASES)
+@pytest.mark.parametrize("n_peers", [1, 7])
+def test_peer_copies_equal_output(hyperion, oracle, kind, path, group_kernel, num_splits, o_dtype, n_peers):
+    dev = torch.device("cuda", 0)
+    wk = _workload(kind, o_dtype)
+    g = wk.to(dev)
+    shape = (g.n_bh * g.seq_q, g.head_dim)
+    o = torch.full(shape, float("nan"), dtype=o_dtype, device=dev)
+    peers = [torch.full(shape, float("nan"), dtype=o_dtype, device=dev) for _ in range(n_peers)]
+    hyperion.read_device_errors(dev, clear=True)
+    hyperion.hyperion_apex_kernel(g.worklist, g.total_work, g.q, None, g.k, None, g.v, g.v_scale, g.ctx_lens,
+                                  g.block_tables, o, g.seq_q, g.head_dim, g.head_dim // 8, g.block_size,
+                                  g.num_blocks, g.inv_sqrt_d, g.causal, path=path, num_splits=num_splits,
+                                  kv_group=wk.kv_group, group_kernel=group_kernel,
+                                  o_peers=[t.data_ptr() for t in peers])
+    torch.cuda.synchronize()
+    assert hyperion.read_device_errors(dev, clear=True) == 0
+    for t in peers:
+        assert torch.equal(t.view(torch.int8) if o_dtype != torch.float32 else t.view(torch.int32),
+                           o.view(torch.int8) if o_dtype != torch.float32 else o.view(torch.int32))
+    o_ref, _, _, _ = oracle.forward_workload_c(wk)
+    ok, mx, mn = oracle.tolerance_check(o.float().cpu().numpy(), o_ref, MAX_ABS, MEAN_ABS)
+    assert ok, f"max {mx:.3e} mean {mn:.3e}"
+
+
+def test_peer_argument_errors(hyperion):
+    dev = torch.device("cuda", 0)
+    g = _workload("decode", torch.bfloat16).to(dev)
+    o = torch.empty(g.n_bh * g.seq_q, g.head_dim, dtype=torch.bfloat16, device=dev)
+    args = (g.worklist, g.total_work, g.q, None, g.k, None, g.v, g.v_scale, g.ctx_lens, g.block_tables, o,
+            g.seq_q, g.head_dim, g.head_dim // 8, g.block_size, g.num_blocks, g.inv_sqrt_d, g.causal)
+    spare = torch.empty(o.numel() + 64, dtype=torch.bfloat16, device=dev)
+    with pytest.raises(RuntimeError, match="at most 7"):
+        hyperion.hyperion_apex_kernel(*args, o_peers=[spare.data_ptr()] * 8)
+    with pytest.raises(RuntimeError, match="16-byte"):
+        hyperion.hyperion_apex_kernel(*args, o_peers=[spare.data_ptr() + 2])
+    with pytest.raises(RuntimeError, match="NULL"):
+        hyperion.hyperion_apex_kernel(*args, o_peers=[0])
+    torch.cuda.synchronize()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _two_gpu_workloads():
+    return [
+        W.make_dense("po2_pre", 2, 4, 256, 256, causal=True, o_dtype=torch.bfloat16, seed=91),
+        W.make_dense("po2_gqa", 2, 8, 1, 2000, o_dtype=torch.float32, seed=92, kv_heads=2),
+        W.make_paged("po2_paged", 3, 5, [40, 900, 3000], page=16, seed=93, o_dtype=torch.bfloat16),
+    ]
+
+
+def _rank_main(rank, world, port, out_dir):
+    import torch.distributed as dist
+
+    import hyperion_b200 as hyperion
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        for i, wk in enumerate(_two_gpu_workloads()):
+            hr = S.head_range(wk.heads, world, rank, wk.kv_group)
+            sub = S.shard_workload(wk, hr).to(dev)
+            rows_max = wk.batch * len(S.head_range(wk.heads, world, 0, wk.kv_group)) * wk.seq_q
+            peer = S.PeerOutput(rows_max, wk.head_dim, wk.o_dtype, dev)
+            try:
+                peer.out.fill_(float("nan"))
+                torch.cuda.synchronize()
+                dist.barrier()
+                o = peer.local[: sub.n_bh * sub.seq_q]
+                hyperion.hyperion_apex_kernel(sub.worklist, sub.total_work, sub.q, None, sub.k, None, sub.v,
+                                              sub.v_scale, sub.ctx_lens, sub.block_tables, o, sub.seq_q,
+                                              sub.head_dim, sub.head_dim // 8, sub.block_size, sub.num_blocks,
+                                              sub.inv_sqrt_d, sub.causal, kv_group=wk.kv_group,
+                                              o_peers=peer.o_peers)
+                dist.barrier()
+                torch.cuda.synchronize()
+                parts = [peer.out[r][: wk.batch * len(S.head_range(wk.heads, world, r, wk.kv_group)) * wk.seq_q]
+                         for r in range(world)]
+                fused = S.assemble_heads(parts, wk.batch, wk.heads, wk.seq_q, world, wk.kv_group)
+                gathered = S.gather_output(o.clone(), wk.batch, wk.heads, wk.seq_q, kv_group=wk.kv_group)
+                same = torch.equal(fused.float(), gathered.float())
+                np.save(os.path.join(out_dir, f"r{rank}_w{i}.npy"), fused.float().cpu().numpy())
+                np.save(os.path.join(out_dir, f"r{rank}_w{i}_same.npy"), np.array([same]))
+                np.save(os.path.join(out_dir, f"r{rank}_w{i}_err.npy"),
+                        np.array([hyperion.read_device_errors(dev, clear=True)]))
+            finally:
+                peer.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_output_over_two_gpus(oracle, tmp_path):
+    world = 2
+    mp.spawn(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    for i, wk in enumerate(_two_gpu_workloads()):
+        o_ref, _, _, _ = oracle.forward_workload_c(wk)
+        for r in range(world):
+            assert np.load(tmp_path / f"r{r}_w{i}_err.npy")[0] == 0
+            assert np.load(tmp_path / f"r{r}_w{i}_same.npy")[0], (wk.name, r)
+            got = np.load(tmp_path / f"r{r}_w{i}.npy")
+            ok, mx, mn = oracle.tolerance_check(got, o_ref, MAX_ABS, MEAN_ABS)
+            assert ok, f"{wk.name} rank {r}: max {mx:.3e} mean {mn:.3e}"
