@@ -178,6 +178,13 @@ _TYPESTR = {torch.float32: ("<f4", torch.float32), torch.float16: ("<f2", torch.
             torch.bfloat16: ("<i2", torch.bfloat16)}
 
 
+def _on(device):
+    """The CUDA device context of `device`, or none for None (the current device)."""
+    import contextlib
+
+    return contextlib.nullcontext() if device is None else torch.cuda.device(device)
+
+
 class PeerOutput:
     """The gathered output [world, rows, D] held in IPC memory on every rank, with
     the other ranks' copies mapped into this process.
@@ -213,15 +220,33 @@ class PeerOutput:
         typestr, view = _TYPESTR[dtype]
         esize = torch.tensor([], dtype=dtype).element_size()
         slot = rows * d * esize
-        with torch.cuda.device(device):
-            self.ptr, handle = ipc_alloc(self.world * slot)
+        # Every step below that can fail on one rank is followed by an exchange of
+        # its outcome, so that all ranks fail together instead of leaving the others
+        # waiting in a collective.
+        self.ptr, handle, why = None, None, None
+        try:
+            with _on(device):
+                self.ptr, handle = ipc_alloc(self.world * slot)
+        except RuntimeError as e:
+            why = str(e)
         handles = [None] * self.world
-        dist.all_gather_object(handles, handle, group=group)
+        dist.all_gather_object(handles, (handle, why), group=group)
         self._opened = []
-        with torch.cuda.device(device):
-            for r in range(self.world):
-                if r != self.rank:
-                    self._opened.append(ipc_open(handles[r]))
+        failed = [(r, w) for r, (_, w) in enumerate(handles) if w is not None]
+        if not failed:  # the same decision on every rank: they all hold the same list
+            try:
+                with _on(device):
+                    for r in range(self.world):
+                        if r != self.rank:
+                            self._opened.append(ipc_open(handles[r][0]))
+            except RuntimeError as e:
+                why = str(e)
+            whys = [None] * self.world
+            dist.all_gather_object(whys, why, group=group)
+            failed = [(r, w) for r, w in enumerate(whys) if w is not None]
+        if failed:
+            self._release(barrier=True)  # every rank takes this branch
+            raise RuntimeError(f"PeerOutput: rank {failed[0][0]}: {failed[0][1]}")
         self.o_peers = [base + self.rank * slot for base in self._opened]
         raw = torch.as_tensor(_DeviceArray(self.ptr, (self.world, rows, d), typestr), device=device)
         self.out = raw.view(view)
@@ -230,17 +255,26 @@ class PeerOutput:
     def close(self) -> None:
         import torch.distributed as dist
 
-        from . import ipc_close, ipc_free
-
         if self.ptr is None:
             return
         torch.cuda.synchronize(self.out.device)
         dist.barrier(group=self.group)
+        self._release(barrier=True)
+
+    def _release(self, barrier: bool = False) -> None:
+        """Unmaps the peers this rank opened and frees its buffer (after a barrier
+        when the peers may still hold mappings of it)."""
+        import torch.distributed as dist
+
+        from . import ipc_close, ipc_free
+
         for base in self._opened:
             ipc_close(base)
         self._opened = []
         self.o_peers = []
-        dist.barrier(group=self.group)
+        if barrier:
+            dist.barrier(group=self.group)
         self.out = self.local = None
-        ipc_free(self.ptr)
-        self.ptr = None
+        if self.ptr is not None:
+            ipc_free(self.ptr)
+            self.ptr = None

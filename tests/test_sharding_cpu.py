@@ -196,3 +196,64 @@ def test_chunked_forward_and_gather_over_two_gloo_ranks(oracle, tmp_path):
     for r in range(world):
         assert np.load(tmp_path / f"chunked_r{r}_n.npy")[0] == 3
         assert np.array_equal(np.load(tmp_path / f"chunked_r{r}.npy"), full), r
+
+
+def _peer_fail_main(rank, world, port, out_dir, fail_at):
+    """PeerOutput's setup with the IPC calls faked: the step named by fail_at fails
+    on rank 1 only, and every rank must raise the same error and release what it
+    allocated and opened."""
+    import json
+
+    import torch.distributed as dist
+
+    import hyperion_b200 as H
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    log = {"freed": [], "closed": [], "opened": []}
+
+    def alloc(nbytes):
+        if fail_at == "alloc" and rank == 1:
+            raise RuntimeError("hyperion_ipc_alloc failed (status 5): out of memory")
+        return 1000 + rank, bytes([rank]) * 64
+
+    def open_(handle):
+        if fail_at == "open" and rank == 1:
+            raise RuntimeError("hyperion_ipc_open failed (status 5): peer access refused")
+        log["opened"].append(handle[0])
+        return 2000 + handle[0]
+
+    H.ipc_alloc, H.ipc_open = alloc, open_
+    H.ipc_close = lambda p: log["closed"].append(p)
+    H.ipc_free = lambda p: log["freed"].append(p)
+    try:
+        try:
+            S.PeerOutput(16, 128, torch.bfloat16, None)
+            log["error"] = None
+        except RuntimeError as e:
+            log["error"] = str(e)
+        with open(os.path.join(out_dir, f"peer_{fail_at}_r{rank}.json"), "w") as f:
+            json.dump(log, f)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fail_at", ["alloc", "open"])
+def test_peer_output_setup_fails_on_every_rank_together(tmp_path, fail_at):
+    import json
+
+    world = 3
+    mp.spawn(_peer_fail_main, args=(world, _free_port(), str(tmp_path), fail_at), nprocs=world, join=True)
+    logs = [json.load(open(tmp_path / f"peer_{fail_at}_r{r}.json")) for r in range(world)]
+    errors = {log["error"] for log in logs}
+    assert len(errors) == 1 and None not in errors, errors
+    assert "rank 1" in errors.pop()
+    for r, log in enumerate(logs):
+        if fail_at == "alloc":
+            assert log["opened"] == [] and log["freed"] == ([] if r == 1 else [1000 + r])
+        else:
+            assert log["freed"] == [1000 + r]
+            assert sorted(log["closed"]) == sorted(2000 + h for h in log["opened"])
+            if r != 1:
+                assert sorted(log["opened"]) == [q for q in range(world) if q != r]
