@@ -64,6 +64,7 @@ struct FwdParams {
   int o_align32;        // 1: O is 32-byte aligned, so a 16-value row piece is whole 32-byte sectors
   long long wait_cycles;  // bound of every device wait: kWaitCycles, shorter only under a test hook
   int fault_stage;        // test hook: index of the KV stage the loading warp leaves unarmed (-1: none)
+  int ticket_group;       // tile kernel: (batch, head) rows per group of its ticket order (0: all rows)
   int n_o_peers;          // copies of O written beside it (0: none)
   void* o_peers[kMaxOutPeers];  // each receives every output element at O's own index
 };

@@ -441,10 +441,15 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
     // [256*(c % cpb), ...) of its bh, and causal cost grows with that position.
     // Tickets walk the positions from the last to the first, all bh at each
     // position, so the most expensive chunks go first and the cheap ones fill
-    // the tail.  Any worklist order stays correct; only the balance depends on it.
+    // the tail.  When the KV of all bh rows would not stay in L2, the bh rows are
+    // taken in groups of p.ticket_group, one group after the other, each walked
+    // that way: the units running at any time then read the KV of one group, which
+    // L2 holds, and the tail still ends on the cheapest chunks.  Any worklist
+    // order stays correct; only the balance and the L2 reuse depend on it.
     const int cpb = max(1, (p.seq_q + kChunk - 1) / kChunk);
     const int groups = (n_chunks + cpb - 1) / cpb;
     const int n_tickets = groups * cpb;
+    const int tg = (p.ticket_group > 0 && p.ticket_group < groups) ? p.ticket_group : groups;
     bool stop = false;
     while (!stop) {
       // Take the next ticket only once every role has started the previous unit:
@@ -457,8 +462,11 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         if (lane == 0) t = (int)atomicAdd(&p.counters[1], 1u);
         t = __shfl_sync(0xffffffffu, t, 0);
         if (t >= n_tickets) break;
-        const int qr = t / groups;
-        const int g = t - qr * groups;
+        const int hg = t / (tg * cpb);                 // group of bh rows
+        const int u = t - hg * (tg * cpb);             // ticket inside the group
+        const int gs = min(tg, groups - hg * tg);      // rows in this group (the last may be short)
+        const int qr = u / gs;
+        const int g = hg * tg + (u - qr * gs);
         const int cand = g * cpb + (cpb - 1 - qr);
         if (cand < n_chunks) {
           c = cand;
@@ -1000,10 +1008,30 @@ inline int setup(int& ctas, int& smem, const char** why) {
   return HYPERION_OK;
 }
 
-inline int launch(const FwdParams& p, int n_sm, int ctas, int smem, cudaStream_t st, int* grid_out) {
+// KV bytes of all bh rows up to which the ticket order keeps every row in one
+// group, and the KV bytes of one group beyond that: both well inside the 126 MB L2,
+// which the Q rows and the O stores pass through as well.
+constexpr double kTicketAllBytes = 96.0 * (1 << 20);
+constexpr double kTicketGroupBytes = 48.0 * (1 << 20);
+
+// bh rows per group of the tile kernel's ticket order (0: one group of all rows),
+// from the KV capacity of a row (its keys at most block_size * num_blocks, K and V
+// bytes per key, shared by kv_group query rows).
+inline int ticket_group(const FwdParams& p) {
   const int n_chunks = (p.total_work + kChunk - 1) / kChunk;
+  const int cpb = std::max(1, (p.seq_q + kChunk - 1) / kChunk);
+  const int rows = (n_chunks + cpb - 1) / cpb;
+  const double per_row = (double)p.block_size * p.num_blocks * (p.head_dim / 8 + p.head_dim) / std::max(p.kv_group, 1);
+  if (per_row <= 0.0 || rows * per_row <= kTicketAllBytes) return 0;
+  return std::max(1, (int)(kTicketGroupBytes / per_row));
+}
+
+inline int launch(const FwdParams& p0, int n_sm, int ctas, int smem, cudaStream_t st, int* grid_out) {
+  const int n_chunks = (p0.total_work + kChunk - 1) / kChunk;
   const int grid = std::min(n_chunks, n_sm * std::max(ctas, 1));
   if (grid <= 0) return HYPERION_OK;
+  FwdParams p = p0;
+  p.ticket_group = ticket_group(p0);
   if (p.debug_scores) {
     tile_fwd_kernel<true><<<grid, kThreads, smem, st>>>(p);
   } else {
