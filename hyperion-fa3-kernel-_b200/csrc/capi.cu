@@ -302,6 +302,8 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
       return fail(HYPERION_ERR_INVALID_ARG, "block_tables numel < n_bh * num_blocks");
   }
   if (workspace == nullptr) return fail(HYPERION_ERR_WORKSPACE, "workspace is NULL");
+  if (workspace_bytes < hyp::kWsPartials)
+    return fail(HYPERION_ERR_WORKSPACE, "workspace smaller than hyperion_workspace_bytes()");
   if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
     return fail(HYPERION_ERR_WORKSPACE, "workspace must be 256-byte aligned");
   if (!worklist || !Q || !K_cache || !V_cache || !V_scale || !context_lens || !O)
@@ -485,12 +487,25 @@ int hyperion_apex_kernel_ex(const int32_t* worklist, int32_t total_work, const u
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "row kernel launch");
   if (ns > 1) {
+    // Programmatic dependent launch: the combine is scheduled while the split kernel
+    // runs (which allows it at its start) and waits on the device for that grid to
+    // finish, instead of the launch starting only after it.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)total_work);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     if (head_dim == 256) {
-      hyp::row::row_combine_kernel<256><<<total_work, 128, 0, st>>>(p);
+      e = cudaLaunchKernelEx(&cfg, hyp::row::row_combine_kernel<256>, p);
     } else {
-      hyp::row::row_combine_kernel<128><<<total_work, 128, 0, st>>>(p);
+      e = cudaLaunchKernelEx(&cfg, hyp::row::row_combine_kernel<128>, p);
     }
-    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
   }
   g_last_call[0] = HYPERION_PATH_ROW;

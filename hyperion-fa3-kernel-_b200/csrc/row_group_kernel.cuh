@@ -253,6 +253,10 @@ __device__ __forceinline__ void drain_stages(uint64_t* full, uint32_t it, long l
 
 template <int D>
 __global__ void __launch_bounds__(kGThreads, group_ctas<D>()) row_group_kernel(FwdParams p, int total_units) {
+  // The split combine kernel is launched as a programmatic dependent of this one:
+  // it may be scheduled now and waits in griddepcontrol.wait until this grid has
+  // finished and its partials are visible, so its launch overlaps this kernel.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   constexpr int W = D / 32;
   constexpr int DPL = D / 32;  // dims per lane
   constexpr int NW = DPL / 4;  // 32-bit words of V bytes per lane and key

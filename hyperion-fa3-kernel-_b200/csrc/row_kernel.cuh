@@ -101,6 +101,10 @@ __device__ __forceinline__ void load_v_lane(const uint8_t* row, int lane, uint32
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdParams p, int total_units) {
+  // The split combine kernel is launched as a programmatic dependent of this one:
+  // it may be scheduled now and waits in griddepcontrol.wait until this grid has
+  // finished and its partials are visible, so its launch overlaps this kernel.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   constexpr int W = D / 32;
   constexpr int DPL = D / 32;  // dims per lane
   constexpr int NW = DPL / 4;  // 32-bit words of V bytes per lane and key
@@ -448,6 +452,9 @@ __global__ void __launch_bounds__(kThreads, kRowCtasPerSm) row_fwd_kernel(FwdPar
 // Merges the n_split partials (m, l, acc[D]) of every item and writes O.
 template <int D>
 __global__ void __launch_bounds__(128) row_combine_kernel(FwdParams p) {
+  // Launched as a programmatic dependent of the split kernel: wait for that grid
+  // to finish and its partials to be visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int item = blockIdx.x;
   const ItemInfo inf = resolve_item(p, item);
   if (!inf.valid) return;

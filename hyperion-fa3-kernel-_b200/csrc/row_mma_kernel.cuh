@@ -305,6 +305,10 @@ __device__ __forceinline__ bool mma_stream(const FwdParams& p, Smem& sm, const C
 
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     row_mma_kernel(FwdParams p, int total_units, const __grid_constant__ CUtensorMap vmap) {
+  // The split combine kernel is launched as a programmatic dependent of this one:
+  // it may be scheduled now and waits in griddepcontrol.wait until this grid has
+  // finished and its partials are visible, so its launch overlaps this kernel.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
