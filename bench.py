@@ -586,6 +586,7 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
     # room beside it.
     gather_total = serial_total = fused_total = 0.0
     fused_why = None
+    gather_checks = None
     if world > 1:
         from hyperion_b200 import sharding as S
 
@@ -648,14 +649,21 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
         # The overlapped output is the serial one, rank by rank (a chunked call may
         # choose other KV splits, so the two agree to rounding, not bit for bit); the
         # fused output is the serial one bit for bit (the same call, stored twice).
+        # Both checks are taken over every rank (a max), so that all ranks agree on the
+        # outcome and take the same collectives after it: a form that disagrees is
+        # reported in the record and left out of its value, not raised on one rank.
         diff = (out_chunks.transpose(0, 1).reshape(out_all.shape).float() - out_all.float()).abs().max().item()
-        if not diff <= 2e-2:
-            raise RuntimeError(f"overlapped gather differs from the serial gather by {diff}")
         fused_same = peer is None or torch.equal(peer.out.view(torch.uint8), out_all.view(torch.uint8))
         if peer is not None:
             peer.close()
-        if not fused_same:
-            raise RuntimeError("the fused gather differs from the serial gather")
+        chk = torch.tensor([diff if diff == diff else float("inf"), 0.0 if fused_same else 1.0],
+                           dtype=torch.float64, device=dev)
+        pg.all_reduce(chk, op=pg.ReduceOp.MAX)
+        gather_checks = {"overlapped_max_abs_diff": float(chk[0]), "fused_bit_exact": bool(chk[1] == 0.0)}
+        if not float(chk[0]) <= 2e-2:
+            gather_total = float("inf")
+        if float(chk[1]) != 0.0:
+            fused_total = float("inf")
         del out_all, out_chunks, peer
 
     vals = torch.tensor([total_ms, e2e_ms, float(pairs), gather_total, serial_total, fused_total],
@@ -712,7 +720,9 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
             rec["hbm_gbs"] = roof["achieved"]
         if world > 1:
             o_bytes = o.numel() * o.element_size()
-            forms = {"overlapped": gather_max, "serial": serial_max}
+            forms = {"serial": serial_max}
+            if gather_max != float("inf"):
+                forms["overlapped"] = gather_max
             if fused_max != float("inf"):
                 forms["fused"] = fused_max
             form = min(forms, key=forms.get)
@@ -723,7 +733,8 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
                 "form": form,
                 "fused_ms_per_step": fused_max / args.steps if "fused" in forms else None,
                 "fused_unavailable": fused_why,
-                "overlapped_ms_per_step": gather_max / args.steps,
+                "checks_against_serial": gather_checks,
+                "overlapped_ms_per_step": gather_max / args.steps if "overlapped" in forms else None,
                 "serial_ms_per_step": serial_max / args.steps,
                 "gather_bytes_received_per_rank": o_bytes * (world - 1),
                 "nvlink_floor_ms": o_bytes * (world - 1) / NVLINK_GBS / 1e6,
