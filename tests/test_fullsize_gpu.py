@@ -149,6 +149,34 @@ def test_decode_gqa_full_size_whole_rows(hyperion, oracle):
     whole_rows_check(hyperion, oracle, wk, bhs)
 
 
+def test_prefill_heads_in_l2_groups_whole_rows(hyperion, oracle):
+    """B2 H96 S4096 causal: 192 (batch, head) rows whose KV (590 KB each, 113 MB in
+    all) does not stay in L2, so the tile kernel's tickets take the rows in groups of
+    85 (48 MB of KV), 85 and 22, each group longest units first.  Every output row
+    is written (O starts as NaN), and whole rows at the group boundaries and in the
+    short last group match the oracle, scores bit for bit."""
+    wk = W.make_dense("l2_groups", 2, 96, 4096, 4096, causal=True, o_dtype=torch.float32, seed=241, device=DEV,
+                      gen_device=DEV, exact=False)
+    assert wk.n_bh * wk.seq_q * 144 > 96 * (1 << 20)
+    o = torch.full((wk.n_bh * wk.seq_q, wk.head_dim), float("nan"), dtype=torch.float32, device=DEV)
+    assert forward(hyperion, wk, o, path="tile") == 0
+    assert hyperion.last_call_info()["path"] == "tile"
+    assert torch.isfinite(o).all(), "a chunk of the ticket order was never taken"
+    bhs = [0, 84, 85, 170, 191]
+    sub, rows = bh_subset(wk, bhs)
+    ref, written, err, _ = oracle.forward_workload_c(sub)
+    assert err == 0 and written.all()
+    ok, mx, mn = oracle.tolerance_check(o.cpu().numpy()[rows], ref[rows_local(sub)], MAX_ABS, MEAN_ABS)
+    assert ok, (mx, mn)
+    wl = items_of(wk, [85, 191], 4096 - 512, 4096)
+    dbg = torch.zeros(wl.shape[0], 4096, dtype=torch.int32, device=DEV)
+    assert forward(hyperion, wk, wk.new_output(), worklist=wl, debug=dbg, path="tile") == 0
+    sub_d, _ = bh_subset(wk, [85, 191], 4096 - 512, 4096)
+    _, _, err, scores = oracle.forward_workload_c(sub_d, scores_ld=4096)
+    assert err == 0
+    assert np.array_equal(dbg.cpu().numpy(), scores)
+
+
 def test_longctx_one_rank_heads_whole_row(hyperion, oracle):
     """B1 S32768 causal, the 8 heads one rank owns at world size 8: the last head's
     32768 query rows against the oracle; scores of the last two 256-row units of the
