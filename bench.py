@@ -584,7 +584,7 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
     # whose gathers (on a second stream) overlap the next run's compute, with the
     # forward's persistent grid kept off GATHER_SMS SMs so that NCCL's kernels find
     # room beside it.
-    gather_total = serial_total = fused_total = 0.0
+    gather_total = serial_total = fused_total = pushed_total = 0.0
     fused_why = None
     gather_checks = None
     if world > 1:
@@ -597,12 +597,12 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
         comm = torch.cuda.Stream(dev)
         budget = max(1, torch.cuda.get_device_properties(dev).multi_processor_count - GATHER_SMS)
 
-        def forward_chunk(items):
+        def forward_chunk(items, out=o, sm_budget=budget):
             wl = wk.worklist[items]
             hyperion.hyperion_apex_kernel(wl, wl.shape[0], wk.q, None, wk.k, None, wk.v, wk.v_scale, wk.ctx_lens,
-                                          wk.block_tables, o, wk.seq_q, wk.head_dim, wk.head_dim // 8, wk.block_size,
-                                          wk.num_blocks, wk.inv_sqrt_d, wk.causal, path=args.path,
-                                          kv_group=wk.kv_group, sm_budget=budget)
+                                          wk.block_tables, out, wk.seq_q, wk.head_dim, wk.head_dim // 8,
+                                          wk.block_size, wk.num_blocks, wk.inv_sqrt_d, wk.causal, path=args.path,
+                                          kv_group=wk.kv_group, sm_budget=sm_budget)
 
         def serial_step():
             call_forward(hyperion, wk, o, path=args.path)
@@ -627,8 +627,21 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
             call_forward(hyperion, wk, peer.local, path=args.path, o_peers=peer.o_peers)
             pg.all_reduce(tick)
 
+        # pushed: the forward in GATHER_CHUNKS runs on every SM into this rank's slot,
+        # each finished run's O rows copied into every peer's gathered buffer by the
+        # copy engines (one stream per peer) while the next run computes, then the
+        # 4-byte all-reduce as the barrier.
+        push_streams = [torch.cuda.Stream(dev) for _ in range(world - 1)]
+
+        def pushed_step():
+            S.forward_and_push(lambda items: forward_chunk(items, out=peer.local, sm_budget=0), chunks, peer,
+                               push_streams)
+            pg.all_reduce(tick)
+
         totals = []
-        for step in (serial_step, overlapped_step, fused_step) if peer is not None else (serial_step, overlapped_step):
+        steps = (serial_step, overlapped_step) + ((fused_step, pushed_step) if peer is not None else ())
+        pushed_diff = None
+        for step in steps:
             step()
             torch.cuda.synchronize()
             g_st = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -644,8 +657,13 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
             torch.cuda.synchronize()
             barrier()
             totals.append(sum(s.elapsed_time(e) for s, e in zip(g_st, g_en)))
+            if step is fused_step:
+                fused_same = torch.equal(peer.out.view(torch.uint8), out_all.view(torch.uint8))
+            if step is pushed_step:
+                pushed_diff = (peer.out.float() - out_all.float()).abs().max().item()
         serial_total, gather_total = totals[:2]
         fused_total = totals[2] if peer is not None else float("inf")
+        pushed_total = totals[3] if peer is not None else float("inf")
         # The overlapped output is the serial one, rank by rank (a chunked call may
         # choose other KV splits, so the two agree to rounding, not bit for bit); the
         # fused output is the serial one bit for bit (the same call, stored twice).
@@ -653,20 +671,25 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
         # outcome and take the same collectives after it: a form that disagrees is
         # reported in the record and left out of its value, not raised on one rank.
         diff = (out_chunks.transpose(0, 1).reshape(out_all.shape).float() - out_all.float()).abs().max().item()
-        fused_same = peer is None or torch.equal(peer.out.view(torch.uint8), out_all.view(torch.uint8))
-        if peer is not None:
+        if peer is None:
+            fused_same, pushed_diff = True, 0.0
+        else:
             peer.close()
-        chk = torch.tensor([diff if diff == diff else float("inf"), 0.0 if fused_same else 1.0],
+        chk = torch.tensor([diff if diff == diff else float("inf"), 0.0 if fused_same else 1.0,
+                            pushed_diff if pushed_diff == pushed_diff else float("inf")],
                            dtype=torch.float64, device=dev)
         pg.all_reduce(chk, op=pg.ReduceOp.MAX)
-        gather_checks = {"overlapped_max_abs_diff": float(chk[0]), "fused_bit_exact": bool(chk[1] == 0.0)}
+        gather_checks = {"overlapped_max_abs_diff": float(chk[0]), "fused_bit_exact": bool(chk[1] == 0.0),
+                         "pushed_max_abs_diff": float(chk[2])}
         if not float(chk[0]) <= 2e-2:
             gather_total = float("inf")
         if float(chk[1]) != 0.0:
             fused_total = float("inf")
+        if not float(chk[2]) <= 2e-2:
+            pushed_total = float("inf")
         del out_all, out_chunks, peer
 
-    vals = torch.tensor([total_ms, e2e_ms, float(pairs), gather_total, serial_total, fused_total],
+    vals = torch.tensor([total_ms, e2e_ms, float(pairs), gather_total, serial_total, fused_total, pushed_total],
                         dtype=torch.float64, device=dev)
     if pg is not None:
         mx = vals.clone()
@@ -674,10 +697,11 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
         sm = vals.clone()
         pg.all_reduce(sm, op=pg.ReduceOp.SUM)
         total_ms_max, e2e_ms_max, gather_max, serial_max = float(mx[0]), float(mx[1]), float(mx[3]), float(mx[4])
-        fused_max = float(mx[5])
+        fused_max, pushed_max = float(mx[5]), float(mx[6])
         pairs_all = float(sm[2])
     else:
         total_ms_max, e2e_ms_max, gather_max, serial_max, fused_max = total_ms, e2e_ms, 0.0, 0.0, 0.0
+        pushed_max = 0.0
         pairs_all = float(pairs)
 
     rec = None
@@ -725,6 +749,8 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
                 forms["overlapped"] = gather_max
             if fused_max != float("inf"):
                 forms["fused"] = fused_max
+            if pushed_max != float("inf"):
+                forms["pushed"] = pushed_max
             form = min(forms, key=forms.get)
             best = forms[form]
             rec["with_gather"] = {
@@ -733,17 +759,21 @@ def measure(hyperion, name, args, rank, world, dev, pg, cpu_budget_s):
                 "form": form,
                 "fused_ms_per_step": fused_max / args.steps if "fused" in forms else None,
                 "fused_unavailable": fused_why,
+                "pushed_ms_per_step": pushed_max / args.steps if "pushed" in forms else None,
                 "checks_against_serial": gather_checks,
                 "overlapped_ms_per_step": gather_max / args.steps if "overlapped" in forms else None,
                 "serial_ms_per_step": serial_max / args.steps,
                 "gather_bytes_received_per_rank": o_bytes * (world - 1),
                 "nvlink_floor_ms": o_bytes * (world - 1) / NVLINK_GBS / 1e6,
-                "mode": ("the fastest of three forms, max over ranks: fused = the forward storing each O row into "
+                "mode": ("the fastest of four forms, max over ranks: fused = the forward storing each O row into "
                          "every rank's gathered buffer as well (peer stores over NVLink into CUDA IPC mappings), then "
-                         f"a 4-byte NCCL all-reduce as the barrier; overlapped = the forward in {GATHER_CHUNKS} runs of "
-                         f"(batch, head) rows on {GATHER_SMS} fewer SMs, each run's O all-gathered (NCCL "
-                         "all_gather_into_tensor, second stream) while the next computes; serial = the forward, then "
-                         "one all-gather"),
+                         "a 4-byte NCCL all-reduce as the barrier; pushed = the forward in "
+                         f"{GATHER_CHUNKS} runs of (batch, head) rows on every SM, each finished run's O rows copied "
+                         "into every peer's gathered buffer by the copy engines (cudaMemcpyAsync over the IPC "
+                         "mappings, one stream per peer) while the next run computes, then the same barrier; "
+                         f"overlapped = the forward in {GATHER_CHUNKS} runs of (batch, head) rows on {GATHER_SMS} "
+                         "fewer SMs, each run's O all-gathered (NCCL all_gather_into_tensor, second stream) while the "
+                         "next computes; serial = the forward, then one all-gather"),
                 "limiter": ("NVLink: each rank receives (world-1) x its O bytes; the floor is that over the measured "
                             f"{NVLINK_GBS:.0f} GB/s peer-copy bandwidth per direction"),
             }

@@ -694,6 +694,13 @@ int hyperion_ipc_free(void* ptr) {
   return e == cudaSuccess ? HYPERION_OK : cuda_fail(e, "cudaFree");
 }
 
+int hyperion_copy_async(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return HYPERION_OK;
+  if (dst == nullptr || src == nullptr) return fail(HYPERION_ERR_INVALID_ARG, "dst or src is NULL");
+  const cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? HYPERION_OK : cuda_fail(e, "cudaMemcpyAsync");
+}
+
 }  // extern "C"
 
 extern "C" int hyperion_apex_kernel_noalloc(const int32_t* worklist, int32_t total_work, const uint32_t* Q,

@@ -379,3 +379,14 @@ def ipc_free(ptr: int) -> None:
     rc = _capi.lib.hyperion_ipc_free(ctypes.c_void_p(ptr))
     if rc != _capi.HYPERION_OK:
         raise RuntimeError(f"hyperion_ipc_free failed (status {rc}): {_capi.last_error()}")
+
+
+def copy_async(dst: int, src: int, nbytes: int, stream=None) -> None:
+    """Copies nbytes from device address src to dst on the copy engines,
+    asynchronously on `stream` (a torch.cuda.Stream; the current stream when None).
+    Either address may be a peer mapping from ipc_open."""
+    st = stream if stream is not None else torch.cuda.current_stream()
+    rc = _capi.lib.hyperion_copy_async(ctypes.c_void_p(dst), ctypes.c_void_p(src), int(nbytes),
+                                       ctypes.c_void_p(st.cuda_stream))
+    if rc != _capi.HYPERION_OK:
+        raise RuntimeError(f"hyperion_copy_async failed (status {rc}): {_capi.last_error()}")

@@ -51,6 +51,7 @@ EXPORTED = (
     "hyperion_ipc_open",
     "hyperion_ipc_close",
     "hyperion_ipc_free",
+    "hyperion_copy_async",
 )
 
 IPC_HANDLE_BYTES = 64  # HYPERION_IPC_HANDLE_BYTES
@@ -144,6 +145,8 @@ def _load() -> ctypes.CDLL:
     lib.hyperion_ipc_close.argtypes = [_vp]
     lib.hyperion_ipc_free.restype = ctypes.c_int
     lib.hyperion_ipc_free.argtypes = [_vp]
+    lib.hyperion_copy_async.restype = ctypes.c_int
+    lib.hyperion_copy_async.argtypes = [_vp, _vp, ctypes.c_size_t, _vp]
     return lib
 
 

@@ -146,6 +146,31 @@ def forward_and_gather(forward_chunk, chunks, o_local: torch.Tensor, out: torch.
     cur.wait_stream(comm)
 
 
+def forward_and_push(forward_chunk, chunks, peer: "PeerOutput", streams) -> None:
+    """Runs the forward chunk by chunk into peer.local and copies each finished
+    chunk's O rows into every other rank's gathered output on the copy engines
+    (PeerOutput.push_rows) while the next chunk computes.
+
+    forward_chunk(items) enqueues the forward of the work items `items` on the
+    current stream with O = peer.local; chunks is a list of (items, O rows) slices
+    such as row_chunks gives.  The copies of a chunk start once its forward is done
+    and run on `streams` (one per peer at most is useful); the current stream waits
+    for all of them before this returns.  Then, as for the fused form, a collective
+    on the current stream of every rank is the barrier after which peer.out holds
+    every rank's rows.  The forward keeps every SM: the copy engines, not kernels,
+    move the rows."""
+    cur = torch.cuda.current_stream(peer.local.device)
+    for items, rows in chunks:
+        forward_chunk(items)
+        done = torch.cuda.Event()
+        done.record(cur)
+        for st in streams:
+            st.wait_event(done)
+        peer.push_rows(rows, streams)
+    for st in streams:
+        cur.wait_stream(st)
+
+
 def gather_output(o_local: torch.Tensor, batch: int, n_heads: int, seq_q: int, group=None,
                   kv_group: int = 1) -> torch.Tensor:
     """All-gathers the head-block outputs of every rank into the full O on each rank.
@@ -248,9 +273,25 @@ class PeerOutput:
             self._release(barrier=True)  # every rank takes this branch
             raise RuntimeError(f"PeerOutput: rank {failed[0][0]}: {failed[0][1]}")
         self.o_peers = [base + self.rank * slot for base in self._opened]
+        self.row_bytes = d * esize
+        self.local_ptr = self.ptr + self.rank * slot
         raw = torch.as_tensor(_DeviceArray(self.ptr, (self.world, rows, d), typestr), device=device)
         self.out = raw.view(view)
         self.local = self.out[self.rank]
+
+    def push_rows(self, rows: slice, streams) -> None:
+        """Copies rows `rows` of `local` into slot `rank` of every other rank's
+        gathered output on the copy engines (hyperion_copy_async over the peer
+        mappings), the peers spread over `streams` (torch.cuda.Stream objects), with
+        no kernel and no SM taken from a forward running beside the copies.  The
+        caller orders each stream after the writes of those rows (an event); the
+        copies are done when the streams are."""
+        from . import copy_async
+
+        n = (rows.stop - rows.start) * self.row_bytes
+        off = rows.start * self.row_bytes
+        for j, dst in enumerate(self.o_peers):
+            copy_async(dst + off, self.local_ptr + off, n, streams[j % len(streams)])
 
     def close(self) -> None:
         import torch.distributed as dist

@@ -218,6 +218,14 @@ int hyperion_ipc_open(const uint8_t* handle, void** ptr);
 int hyperion_ipc_close(void* ptr);
 int hyperion_ipc_free(void* ptr);
 
+/* Copies `bytes` from src to dst on the copy engines, asynchronously on `stream`
+ * (cudaMemcpyAsync, either address this device's memory or a peer mapping from
+ * hyperion_ipc_open).  It moves the rows of a finished piece of a head-sharded
+ * forward into every rank's gathered output while the next piece computes, with no
+ * kernel of its own and no SM taken from the forward.  No counterpart in the
+ * reference. */
+int hyperion_copy_async(void* dst, const void* src, size_t bytes, void* stream);
+
 /* Last CUDA error string seen by the library on this thread ("" if none). */
 const char* hyperion_last_error_string(void);
 

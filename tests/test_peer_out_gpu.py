@@ -5,7 +5,9 @@ row with and without KV splits, both grouped kernels) must leave each of them eq
 to O, bit for bit, and O itself must still meet the oracle bar.  On two GPUs,
 PeerOutput maps each rank's gathered buffer into the other rank and the forward
 stores its head block into both; the result must equal the NCCL all-gather of the
-same blocks, bit for bit.
+same blocks, bit for bit.  The same blocks moved by the copy engines
+(sharding.forward_and_push: the forward in runs, each run's rows pushed into the
+other rank's buffer) must meet the oracle bar on every rank.
 """
 import os
 import socket
@@ -91,6 +93,23 @@ def test_peer_argument_errors(hyperion):
     torch.cuda.synchronize()
 
 
+def test_copy_async_moves_bytes(hyperion):
+    # hyperion_copy_async between two buffers of this device, at offsets and sizes
+    # that are not multiples of anything, on a side stream; a NULL address is refused.
+    dev = torch.device("cuda", 0)
+    src = torch.randint(0, 256, (1 << 20,), dtype=torch.uint8, device=dev)
+    dst = torch.zeros_like(src)
+    st = torch.cuda.Stream(dev)
+    st.wait_stream(torch.cuda.current_stream(dev))
+    for off, n in ((0, 1 << 20), (7, 1000), (4097, 65531), (1 << 19, 0)):
+        hyperion.copy_async(dst.data_ptr() + off, src.data_ptr() + off, n, st)
+    torch.cuda.current_stream(dev).wait_stream(st)
+    torch.cuda.synchronize()
+    assert torch.equal(dst, src)
+    with pytest.raises(RuntimeError):
+        hyperion.copy_async(0, src.data_ptr(), 16)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -140,6 +159,29 @@ def _rank_main(rank, world, port, out_dir):
                 same = torch.equal(fused.float(), gathered.float())
                 np.save(os.path.join(out_dir, f"r{rank}_w{i}.npy"), fused.float().cpu().numpy())
                 np.save(os.path.join(out_dir, f"r{rank}_w{i}_same.npy"), np.array([same]))
+                # The same blocks through the copy engines: the forward in runs of
+                # (batch, head) rows into `local`, each run pushed into the other
+                # rank's buffer while the next computes (sharding.forward_and_push).
+                peer.out.fill_(float("nan"))
+                torch.cuda.synchronize()
+                dist.barrier()
+                n_chunks = next(c for c in (3, 2, 1) if sub.n_bh % c == 0)
+
+                def fwd(items):
+                    wl = sub.worklist[items]
+                    hyperion.hyperion_apex_kernel(wl, wl.shape[0], sub.q, None, sub.k, None, sub.v, sub.v_scale,
+                                                  sub.ctx_lens, sub.block_tables, o, sub.seq_q, sub.head_dim,
+                                                  sub.head_dim // 8, sub.block_size, sub.num_blocks, sub.inv_sqrt_d,
+                                                  sub.causal, kv_group=wk.kv_group)
+
+                streams = [torch.cuda.Stream(dev) for _ in range(world - 1)]
+                S.forward_and_push(fwd, S.row_chunks(sub, n_chunks), peer, streams)
+                dist.barrier()
+                torch.cuda.synchronize()
+                parts = [peer.out[r][: wk.batch * len(S.head_range(wk.heads, world, r, wk.kv_group)) * wk.seq_q]
+                         for r in range(world)]
+                pushed = S.assemble_heads(parts, wk.batch, wk.heads, wk.seq_q, world, wk.kv_group)
+                np.save(os.path.join(out_dir, f"r{rank}_w{i}_pushed.npy"), pushed.float().cpu().numpy())
                 np.save(os.path.join(out_dir, f"r{rank}_w{i}_err.npy"),
                         np.array([hyperion.read_device_errors(dev, clear=True)]))
             finally:
@@ -160,3 +202,7 @@ def test_peer_output_over_two_gpus(oracle, tmp_path):
             got = np.load(tmp_path / f"r{r}_w{i}.npy")
             ok, mx, mn = oracle.tolerance_check(got, o_ref, MAX_ABS, MEAN_ABS)
             assert ok, f"{wk.name} rank {r}: max {mx:.3e} mean {mn:.3e}"
+            pushed = np.load(tmp_path / f"r{r}_w{i}_pushed.npy")
+            assert not np.isnan(pushed).any(), (wk.name, r)
+            ok, mx, mn = oracle.tolerance_check(pushed, o_ref, MAX_ABS, MEAN_ABS)
+            assert ok, f"{wk.name} rank {r} pushed: max {mx:.3e} mean {mn:.3e}"
