@@ -110,6 +110,49 @@ def test_copy_async_moves_bytes(hyperion):
         hyperion.copy_async(0, src.data_ptr(), 16)
 
 
+class _LocalPeers:
+    """The attributes of sharding.PeerOutput that forward_and_push reads, with
+    buffers of this device standing in for the other ranks' gathered outputs."""
+
+    def __init__(self, rows, d, dtype, n_peers, dev):
+        self.local = torch.full((rows, d), float("nan"), dtype=dtype, device=dev)
+        self.peers = [torch.full((rows, d), float("nan"), dtype=dtype, device=dev) for _ in range(n_peers)]
+        self.row_bytes = d * self.local.element_size()
+        self.local_ptr = self.local.data_ptr()
+        self.o_peers = [t.data_ptr() for t in self.peers]
+
+    push_rows = S.PeerOutput.push_rows
+
+
+@pytest.mark.parametrize("kind,path,n_chunks,n_peers,n_streams", [
+    ("prefill", "tile", 3, 7, 7), ("prefill", "row", 2, 1, 1), ("decode", "row", 4, 3, 2), ("gqa", "row", 3, 2, 2)])
+def test_forward_and_push_on_one_gpu(hyperion, oracle, kind, path, n_chunks, n_peers, n_streams):
+    # The forward in runs of (batch, head) rows, each run's rows copied into every
+    # "peer" buffer by the copy engines while the next run computes: every peer
+    # buffer ends equal to the local output, which meets the oracle bar.
+    dev = torch.device("cuda", 0)
+    wk = _workload(kind, torch.bfloat16)
+    g = wk.to(dev)
+    peer = _LocalPeers(g.n_bh * g.seq_q, g.head_dim, torch.bfloat16, n_peers, dev)
+
+    def fwd(items):
+        wl = g.worklist[items]
+        hyperion.hyperion_apex_kernel(wl, wl.shape[0], g.q, None, g.k, None, g.v, g.v_scale, g.ctx_lens,
+                                      g.block_tables, peer.local, g.seq_q, g.head_dim, g.head_dim // 8, g.block_size,
+                                      g.num_blocks, g.inv_sqrt_d, g.causal, path=path, kv_group=wk.kv_group)
+
+    hyperion.read_device_errors(dev, clear=True)
+    streams = [torch.cuda.Stream(dev) for _ in range(n_streams)]
+    S.forward_and_push(fwd, S.row_chunks(g, n_chunks), peer, streams)
+    torch.cuda.synchronize()
+    assert hyperion.read_device_errors(dev, clear=True) == 0
+    for t in peer.peers:
+        assert torch.equal(t.view(torch.int16), peer.local.view(torch.int16))
+    o_ref, _, _, _ = oracle.forward_workload_c(wk)
+    ok, mx, mn = oracle.tolerance_check(peer.local.float().cpu().numpy(), o_ref, MAX_ABS, MEAN_ABS)
+    assert ok, f"max {mx:.3e} mean {mn:.3e}"
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
