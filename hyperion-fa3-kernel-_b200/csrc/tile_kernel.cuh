@@ -352,6 +352,40 @@ __device__ __forceinline__ float row_half_p(uint32_t s_col, const uint32_t (&mk)
   return l.x + l.y;
 }
 
+// Chunks of a masked 64-key half that the warp computes: one past the last 16-key
+// chunk in which any of its 32 rows attends a key (a warp-uniform count, 0-4).  On
+// the causal diagonal the later chunks are masked for every row of a warp: for the
+// first Q tile of a unit the whole last tile, and three chunks in eight of its
+// diagonal tile on average.
+__device__ __forceinline__ int half_chunks(const uint32_t (&mk)[4], int c0, int kbase, int row_end) {
+  int n = 0;
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    if (__any_sync(0xffffffffu, chunk_bits(mk, c0 + c, kbase, row_end) != 0u)) n = c + 1;
+  return n;
+}
+
+// The masked half with only its first `nch` chunks computed (nch < 4), one chunk
+// after the other; the weights of the other chunks are zero, stored over their S
+// columns.  Returns sum(P).
+__device__ __noinline__ float row_half_p_prefix(uint32_t s_col, const uint32_t (&mk)[4], int c0, int kbase,
+                                               int row_end, const PExp& x, int nch) {
+  float2 l = make_float2(0.f, 0.f);
+#pragma unroll 1
+  for (int h = 0; h < nch; ++h) {
+    uint32_t v[16];
+    float e[16];
+    tc::ld16(s_col + 16 * h, v);
+    tc::ld_wait_regs(v);
+    p_exp16(v, x, e);
+    p_step<true, false>(s_col, h, e, chunk_bits(mk, c0 + h, kbase, row_end), v, e, x, l);
+  }
+  const uint32_t z[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+#pragma unroll 1
+  for (int h = nch; h < 4; ++h) tc::st8(s_col + 8 * h, z);
+  return l.x + l.y;
+}
+
 // O row *= alpha (lanes that need no rescale pass alpha = 1).
 __device__ __forceinline__ void rescale_row(uint32_t o_col, float alpha) {
 #pragma unroll 1
@@ -933,7 +967,13 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
         x.k2 = k2;
         x.bias = -(float)s_m * k2;
         // ---- half A: keys 0-63, P over S columns 0-31
-        l += wfa ? row_half_p<false>(s_col, mk, 0, k0, row_end, x) : row_half_p<true>(s_col, mk, 0, k0, row_end, x);
+        if (wfa) {
+          l += row_half_p<false>(s_col, mk, 0, k0, row_end, x);
+        } else {
+          const int nch = half_chunks(mk, 0, k0, row_end);
+          l += nch == 4 ? row_half_p<true>(s_col, mk, 0, k0, row_end, x)
+                        : row_half_p_prefix(s_col, mk, 0, k0, row_end, x, nch);
+        }
         tc::st_wait();
         tc::fence_before_sync();
         __syncwarp();
@@ -946,8 +986,13 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
           }
           tc::fence_after_sync();
         }
-        l += wfb ? row_half_p<false>(s_col + 64, mk, 4, k0, row_end, x)
-                 : row_half_p<true>(s_col + 64, mk, 4, k0, row_end, x);
+        if (wfb) {
+          l += row_half_p<false>(s_col + 64, mk, 4, k0, row_end, x);
+        } else {
+          const int nch = half_chunks(mk, 4, k0, row_end);
+          l += nch == 4 ? row_half_p<true>(s_col + 64, mk, 4, k0, row_end, x)
+                        : row_half_p_prefix(s_col + 64, mk, 4, k0, row_end, x, nch);
+        }
         tc::st_wait();
         tc::fence_before_sync();
         __syncwarp();
