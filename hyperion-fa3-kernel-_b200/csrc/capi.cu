@@ -231,7 +231,7 @@ size_t workspace_needed(const DevInfo& di, int total_work, int D, int block_size
 
 extern "C" {
 
-int32_t hyperion_version(void) { return 1 * 10000 + 3 * 100 + 0; }
+int32_t hyperion_version(void) { return 1 * 10000 + 4 * 100 + 0; }
 
 const char* hyperion_last_error_string(void) { return g_last_error.c_str(); }
 

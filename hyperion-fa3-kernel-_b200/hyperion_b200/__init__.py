@@ -52,7 +52,7 @@ from ._capi import (  # noqa: F401
 )
 
 HYPERION_LOADED = True
-__version__ = "1.3.0"
+__version__ = "1.4.0"
 
 _O_DTYPES = {torch.float16: _capi.DTYPE_F16, torch.bfloat16: _capi.DTYPE_BF16, torch.float32: _capi.DTYPE_F32}
 _PATHS = {"auto": _capi.PATH_AUTO, "row": _capi.PATH_ROW, "tile": _capi.PATH_TILE}

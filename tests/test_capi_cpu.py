@@ -31,7 +31,7 @@ def test_library_loads_and_exports_every_declared_symbol(hyperion):
     lib = ctypes.CDLL(hyperion.library_path())
     for name in _declared_functions():
         assert hasattr(lib, name), name
-    assert lib.hyperion_version() == 10300
+    assert lib.hyperion_version() == 10400
 
 
 def test_drop_in_names_match_reference_module(hyperion):
