@@ -223,7 +223,7 @@ int hyperion_ipc_free(void* ptr);
  * hyperion_ipc_open).  It moves the rows of a finished piece of a head-sharded
  * forward into every rank's gathered output while the next piece computes, with no
  * kernel of its own and no SM taken from the forward.  No counterpart in the
- * reference. */
+ * reference.  Added in version 1.4.0. */
 int hyperion_copy_async(void* dst, const void* src, size_t bytes, void* stream);
 
 /* Last CUDA error string seen by the library on this thread ("" if none). */
