@@ -684,17 +684,26 @@ __global__ void __launch_bounds__(kThreads, 1) tile_fwd_kernel(FwdParams p) {
       if (u.kind == 0) break;
       if (u.n_tiles == 0) continue;
       // ---- Q rows of the unit -> e4m3 +-1, K-major SW128 (a negative inv_sqrt_d is
-      // folded in by flipping every bit: the scores change sign)
-      if (!mbar_wait_warp(&sm.q_empty, (uq & 1) ^ 1, abort, p.err)) break;
+      // folded in by flipping every bit: the scores change sign).  The work items and
+      // the sign bits are loaded before the wait for the Q buffer: the converters
+      // reach this point tiles before the last QK of the previous unit frees it, so
+      // the two dependent global reads are done by then instead of delaying the
+      // next unit's first QK.
+      uint4 qbits[kQTiles];
 #pragma unroll
       for (int i = 0; i < kQTiles; ++i) {
         const int r = i * kRows + ct;
-        uint4 bits = make_uint4(0u, 0u, 0u, 0u);
+        qbits[i] = make_uint4(0u, 0u, 0u, 0u);
         if (r >= u.seg_lo && r < u.seg_hi) {
           const int qi = __ldg(&p.worklist[u.entry0 + r].x);
           if (qi >= 0 && qi < p.seq_q)
-            bits = __ldg(reinterpret_cast<const uint4*>(p.q + ((long long)u.bh * p.seq_q + qi) * 4));
+            qbits[i] = __ldg(reinterpret_cast<const uint4*>(p.q + ((long long)u.bh * p.seq_q + qi) * 4));
         }
+      }
+      if (!mbar_wait_warp(&sm.q_empty, (uq & 1) ^ 1, abort, p.err)) break;
+#pragma unroll
+      for (int i = 0; i < kQTiles; ++i) {
+        uint4 bits = qbits[i];
         if (p.inv_sqrt_d < 0.f) bits = make_uint4(~bits.x, ~bits.y, ~bits.z, ~bits.w);
         const uint32_t words[4] = {bits.x, bits.y, bits.z, bits.w};
         const uint32_t tb = q_base + i * (kRows * 128);
